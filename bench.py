@@ -1,0 +1,374 @@
+#!/usr/bin/env python
+"""Benchmark of the Quartet-II NVFP4 linear hot path on B200.
+
+Workload (the one its headline metric is quoted on):
+the CloverLM-4B linear set -- QKV 3584->10752, attention output 3584->3584,
+MLP up 3584->14336, MLP down 14336->3584 -- at M = 65536 tokens per GPU.
+One step = forward + backward of all four Quartet-II linears through the
+public API (Quartet_II_linear), i.e. abs-max, four-over-six quantization,
+NVFP4 GEMM, randomized-Hadamard EDEN quantization of E and E^T,
+requantization of W^T and X^T, dgrad and wgrad NVFP4 GEMMs.  On N > 1 GPUs
+each rank runs its own 65536 tokens (weak scaling) and the bf16 weight
+gradients are all-reduced (NCCL, AVG) as the data-parallel exchange step.
+
+FLOP per step per GPU = 6 * M * sum(K*N) = 60.6 TFLOP.  Inputs are synthetic
+(seeded N(0,1) activations/gradients, N(0, 0.02) weights) and larger than L2.
+
+`--impl reference` times the reference algorithm on the host cores instead:
+the CPU restatement in oracle/ (the reference's own implementation is CUDA
+plus a Triton emulation, neither of which runs on host cores), on a bounded
+token sample of the same four linears.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SHAPES = [("qkv", 3584, 10752), ("attn_out", 3584, 3584), ("mlp_up", 3584, 14336), ("mlp_down", 14336, 3584)]
+METRIC = "Quartet-II linear fwd+bwd TFLOP/s at 4B shapes; train tokens/s at 1/2/4/8"
+UNIT = "TFLOP/s"
+KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2b_rht_eden_dual": 3,
+                    "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1}
+
+
+def flops_per_token() -> float:
+    return 6.0 * sum(k * n for _, k, n in SHAPES)
+
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p.get("hbm_gbs", 6650.0), "bf16_tflops": p.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", 1400.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampler running during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        loaded = [s for s in sm if s > 500] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------ CPU (oracle)
+
+def cpu_step_tokens() -> int:
+    return int(os.environ.get("Q2B_CPU_SAMPLE_TOKENS", "128"))
+
+
+def run_cpu_sample(tokens: int, seed: int = 0):
+    """One fwd+bwd of the four linears on `tokens` tokens with the CPU oracle.
+    Returns (seconds, flops)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(seed)
+    h16 = oracle.hadamard128_bf16()[:16].copy()
+    t_total = 0.0
+    for i, (_, K, N) in enumerate(SHAPES):
+        x = oracle.f32_to_bf16(rng.standard_normal((tokens, K), dtype=np.float32))
+        w = oracle.f32_to_bf16((0.02 * rng.standard_normal((N, K))).astype(np.float32))
+        dy = oracle.f32_to_bf16(rng.standard_normal((tokens, N), dtype=np.float32))
+        t0 = time.perf_counter()
+        oracle.linear_fwd_bwd(x, w, dy, h16, seeds=(4 * i + 1, 4 * i + 2, 4 * i + 3, 4 * i + 4))
+        t_total += time.perf_counter() - t0
+    return t_total, flops_per_token() * tokens
+
+
+def cpu_baseline_entry(tokens: int, reps: int = 1) -> dict:
+    import oracle
+    secs, flops = 0.0, 0.0
+    for r in range(reps):
+        s, f = run_cpu_sample(tokens, seed=r)
+        secs += s
+        flops += f
+    return {"value": flops / secs / 1e12, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"fwd+bwd of the four 4B linears on {tokens} tokens x {reps} (oracle/ C restatement, "
+                      f"{oracle.num_threads()} threads; GEMMs as fp32 numpy matmuls)"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    tokens = cpu_step_tokens()
+    for _ in range(args.warmup):
+        run_cpu_sample(tokens)
+    secs, flops = 0.0, 0.0
+    for k in range(args.steps):
+        s, f = run_cpu_sample(tokens, seed=k + 1)
+        secs += s
+        flops += f
+    value = flops / secs / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "4B Quartet-II linear set fwd+bwd (QKV 3584->10752, O 3584->3584, "
+                               "up 3584->14336, down 14336->3584)", "tokens_per_step": tokens,
+                   "note": "bounded token sample on host cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"{tokens} tokens per step, oracle/ C restatement on {oracle.num_threads()} "
+                                   f"host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- GPU
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import cloverlm_b200
+    from cloverlm_b200 import _lib
+    from cloverlm_b200 import linear as L
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    _lib.load(build_if_missing=False)
+
+    M = args.tokens
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layers, xs, dys = [], [], []
+    for name, K, N in SHAPES:
+        lay = L.Quartet_II_linear(K, N, bias=False, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            lay.weight.normal_(0.0, 0.02, generator=torch.Generator(device=dev).manual_seed(99 + K + N))
+        layers.append(lay)
+        xs.append(torch.randn(M, K, device=dev, dtype=torch.bfloat16, generator=g).requires_grad_(True))
+        dys.append(torch.randn(M, N, device=dev, dtype=torch.bfloat16, generator=g))
+
+    comm = None
+    if world > 1:
+        from cloverlm_b200.ddp import GradAllReduce
+        comm = GradAllReduce([lay.weight for lay in layers])
+
+    # bench-only instrumentation: kernel launches and GEMM launch durations
+    counters = {"launches": 0, "gemm_events": []}
+    orig_call = _lib.call
+    state = {"timing": False}
+
+    def counting_call(name, *a):
+        if state["timing"]:
+            counters["launches"] += KERNELS_PER_CALL.get(name, 0)
+        return orig_call(name, *a)
+
+    _lib.call = counting_call
+    orig_mm = L._fp4_mm
+
+    def timed_mm(x_fp4, w_fp4, x_mx, w_mx, alpha):
+        if not state["timing"]:
+            return orig_mm(x_fp4, w_fp4, x_mx, w_mx, alpha)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = orig_mm(x_fp4, w_fp4, x_mx, w_mx, alpha)
+        e.record()
+        counters["gemm_events"].append((s, e, 2.0 * x_fp4.shape[0] * w_fp4.shape[0] * x_fp4.shape[1] * 2))
+        return out
+
+    L._fp4_mm = timed_mm
+
+    def step():
+        for lay, x, dy in zip(layers, xs, dys):
+            lay.weight.grad = None
+            x.grad = None
+            y = lay(x.view(1, M, -1))
+            y.backward(dy.view(1, M, -1))
+        if comm is not None:
+            comm.wait()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    state["timing"] = True
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    state["timing"] = False
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    gemm_ms = sum(s.elapsed_time(e) for s, e, _ in counters["gemm_events"])
+    gemm_flops = sum(f for _, _, f in counters["gemm_events"])
+    n_gemm = len(counters["gemm_events"])
+    launches = counters["launches"] // args.steps
+
+    # ---- end to end: inputs from pinned host memory, result read back, every step
+    host_x = [x.detach().cpu().pin_memory() for x in xs]
+    host_dy = [dy.cpu().pin_memory() for dy in dys]
+    h2d = sum(t.numel() * t.element_size() for t in host_x + host_dy)
+    res_host = torch.empty(len(layers), dtype=torch.float32).pin_memory()
+    d2h = res_host.numel() * res_host.element_size()
+
+    def e2e_step():
+        norms = []
+        for lay, hx, hdy in zip(layers, host_x, host_dy):
+            x = hx.to(dev, non_blocking=True).requires_grad_(True)
+            dy = hdy.to(dev, non_blocking=True)
+            lay.weight.grad = None
+            y = lay(x.view(1, M, -1))
+            y.backward(dy.view(1, M, -1))
+            norms.append(lay.weight.grad.float().norm())
+        if comm is not None:
+            comm.wait()
+        res_host.copy_(torch.stack(norms), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    if comm is not None:
+        comm.close()
+
+    flops_step = flops_per_token() * M
+    value = world * flops_step / (ms / 1e3) / 1e12
+    peaks = load_peaks()
+    fp4_peak = 4.0 * peaks["bf16_tflops_sustained"]
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e4m3 block-16, fp32 accumulate, bf16 io)",
+        "data": "synthetic (seeded N(0,1) activations and gradients, N(0,0.02) weights)",
+        "config": {"workload": "4B Quartet-II linear set fwd+bwd: QKV 3584->10752, O 3584->3584, "
+                               "up 3584->14336, down 14336->3584 (BASELINE config 3)",
+                   "tokens_per_gpu": M, "tokens_per_s": world * M / (ms / 1e3),
+                   "parallelism": f"dp{world}", "allreduce": "bf16 NCCL AVG" if world > 1 else None,
+                   "l2": "inputs larger than L2 (>= 470 MB per operand)"},
+        "e2e": {"value": world * flops_step / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "Quartet_II_linear API; activations and output gradients copied from pinned host "
+                        "memory each step, weight-gradient norms read back"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_nvfp4_kernel", "achieved": achieved,
+                     "peak": fp4_peak, "unit": "TFLOP/s",
+                     "frac": (achieved / fp4_peak) if achieved else None, "traffic": None,
+                     "peak_note": "dense NVFP4 = 4 x measured sustained bf16 (MEASURED_PEAKS.json "
+                                  f"{peaks['source']}); nominal dense fp4 9000 TFLOP/s",
+                     "gemm_launches_per_step": n_gemm // max(args.steps, 1),
+                     "gemm_share_of_step": (gemm_ms / args.steps) / ms},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "lib": _lib.lib_path(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_entry(cpu_step_tokens())
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,386 @@
+// libq2b: host side of the C ABI declared in include/q2b.h.  The whole
+// library is one translation unit (kernels are header-only .cuh files).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/q2b.h"
+#include "common.cuh"
+#include "gemm_nvfp4.cuh"
+#include "quant_fwd.cuh"
+#include "rht_eden.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define Q2B_CUDA(call)                                                                               \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess) {                                                                         \
+      cudaGetLastError();                                                                            \
+      return fail(Q2B_ERR_CUDA, "%s failed: %s (%s)", #call, cudaGetErrorName(e_), cudaGetErrorString(e_)); \
+    }                                                                                                \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#define Q2B_REQUIRE_PTR(p)                                                                          \
+  do {                                                                                              \
+    if ((p) == nullptr) return fail(Q2B_ERR_INVALID, "Pointer `%s` is null", #p);                   \
+    if (!aligned16(p)) return fail(Q2B_ERR_INVALID, "Pointer `%s` is not aligned to 16 bytes", #p); \
+  } while (0)
+
+#define Q2B_REQUIRE_NONNULL(p) \
+  do {                         \
+    if ((p) == nullptr) return fail(Q2B_ERR_INVALID, "Pointer `%s` is null", #p); \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+template <typename K>
+cudaError_t set_smem(K kernel, uint32_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+// One-time per-device setup: device properties, kernel shared-memory limits,
+// the driver's tensor-map encoder.
+int device_setup(int* dev_out, int* sms_out) {
+  int dev = 0;
+  Q2B_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(Q2B_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    Q2B_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    Q2B_CUDA(cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+    Q2B_CUDA(cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (d.cc_major != 10 || d.cc_minor != 0)
+      return fail(Q2B_ERR_DEVICE, "libq2b is built for sm_100a; device %d is sm_%d%d", dev, d.cc_major, d.cc_minor);
+    if (g_encode == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      Q2B_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+      if (fn == nullptr || q != cudaDriverEntryPointSuccess)
+        return fail(Q2B_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    using namespace q2b;
+    Q2B_CUDA(set_smem(rht_eden_kernel<kInBf16, kOutRows>, RhtCfg<kInBf16, kOutRows>::kSmemBytes));
+    Q2B_CUDA(set_smem(rht_eden_kernel<kInBf16, kOutCols>, RhtCfg<kInBf16, kOutCols>::kSmemBytes));
+    Q2B_CUDA(set_smem(rht_eden_kernel<kInBf16, kOutBoth>, RhtCfg<kInBf16, kOutBoth>::kSmemBytes));
+    Q2B_CUDA(set_smem(rht_eden_kernel<kInFp4, kOutCols>, RhtCfg<kInFp4, kOutCols>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256>, GemmCfg<256>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128>, GemmCfg<128>::kSmemBytes));
+    d.ready = true;
+  }
+  *dev_out = dev;
+  *sms_out = d.sms;
+  return Q2B_OK;
+}
+
+// 2-D tensor map over a row-major [rows, inner] matrix with a box of
+// box_inner x box_rows elements and the 128-byte swizzle.
+int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+              uint64_t rows, uint32_t box_inner, uint32_t box_rows) {
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q2B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return Q2B_OK;
+}
+
+int check_dims128(const char* what, int64_t a, int64_t b) {
+  if (a <= 0 || b <= 0) return fail(Q2B_ERR_INVALID, "%s: dimensions must be positive (got %lld x %lld)", what,
+                                    static_cast<long long>(a), static_cast<long long>(b));
+  if (a % 128 != 0) return fail(Q2B_ERR_INVALID, "%s: rows must be divisible by 128 (got %lld)", what,
+                                static_cast<long long>(a));
+  if (b % 128 != 0) return fail(Q2B_ERR_INVALID, "%s: cols must be divisible by 128 (got %lld)", what,
+                                static_cast<long long>(b));
+  if (a * b / 8 >= (int64_t(1) << 40)) return fail(Q2B_ERR_INVALID, "%s: tensor too large", what);
+  return Q2B_OK;
+}
+
+int launch_sr(void* sf, float* ts, const void* scratch, const unsigned* maxp, float fp8_max, uint64_t seed,
+              int64_t nscales, int sms, cudaStream_t st) {
+  const int64_t n8 = nscales / 8;
+  const int64_t want = (n8 + 255) / 256;
+  const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
+  q2b::sr_scales_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<uint2*>(sf), ts,
+                                                 reinterpret_cast<const uint4*>(scratch), maxp, 1.f / fp8_max, seed,
+                                                 n8);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+}  // namespace
+
+namespace {
+
+int rht_check_h(const void* h, int h_rows) {
+  Q2B_REQUIRE_PTR(h);
+  if (h_rows != 16 && h_rows != 128)
+    return fail(Q2B_ERR_INVALID, "rotation matrix must have 16 (Hadamard slice) or 128 rows, got %d", h_rows);
+  return Q2B_OK;
+}
+
+template <int kIn, int kOut>
+int launch_rht(const CUtensorMap& tmap, const q2b::RhtParams& p, int sms, cudaStream_t st) {
+  using Cfg = q2b::RhtCfg<kIn, kOut>;
+  const int64_t ntiles = (p.M / 128) * (p.N / 128);
+  const int grid = static_cast<int>(ntiles < sms ? ntiles : sms);
+  q2b::rht_eden_kernel<kIn, kOut><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tmap, p);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q2b_version(void) { return 100; }
+
+const char* q2b_last_error(void) { return g_err; }
+
+int q2b_device_status(unsigned* code) {
+  Q2B_REQUIRE_NONNULL(code);
+  Q2B_CUDA(cudaDeviceSynchronize());
+  unsigned v = 0, zero = 0;
+  Q2B_CUDA(cudaMemcpyFromSymbol(&v, q2b::g_watchdog, sizeof(unsigned)));
+  Q2B_CUDA(cudaMemcpyToSymbol(q2b::g_watchdog, &zero, sizeof(unsigned)));
+  *code = v;
+  return Q2B_OK;
+}
+
+int q2b_abs_max(float* out, const void* x, int64_t n, void* stream) {
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(out);
+  if (n <= 0) return fail(Q2B_ERR_INVALID, "abs_max: n must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Q2B_CUDA(cudaMemsetAsync(out, 0, sizeof(float), st));
+  const int64_t nvec = n / 8;
+  const int64_t want = (nvec + 255) / 256;
+  const int blocks = static_cast<int>(want < 1 ? 1 : (want < int64_t(sms) * 8 ? want : int64_t(sms) * 8));
+  q2b::abs_max_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<unsigned*>(out), static_cast<const uint4*>(x), nvec,
+                                              static_cast<const uint16_t*>(x) + nvec * 8, n - nvec * 8);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                  int64_t rows, int64_t cols, int mode, void* stream) {
+  if (mode != Q2B_MODE_RNE && mode != Q2B_MODE_FOUR_SIX)
+    return fail(Q2B_ERR_INVALID, "quant_fwd: unknown mode %d", mode);
+  const char* name = mode == Q2B_MODE_RNE ? "rtn_fp4" : "four_six_fp4";
+  if (cols % 128 != 0) return fail(Q2B_ERR_INVALID, "%s: cols must be divisible by 128", name);
+  if (int r = check_dims128(name, rows, cols)) return r;
+  Q2B_REQUIRE_PTR(codes);
+  Q2B_REQUIRE_PTR(sf);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(ts);
+  Q2B_REQUIRE_NONNULL(amax);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t nvecs = rows * cols / 8;
+  const int64_t per_block = int64_t(q2b::kQuantThreads) * q2b::kQuantUnroll;
+  const int64_t want = (nvecs + per_block - 1) / per_block;
+  const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
+  if (mode == Q2B_MODE_FOUR_SIX)
+    q2b::quant_fwd_kernel<true><<<blocks, q2b::kQuantThreads, 0, st>>>(
+        static_cast<uint32_t*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint4*>(x), amax,
+        scale_override, nvecs, cols / 16);
+  else
+    q2b::quant_fwd_kernel<false><<<blocks, q2b::kQuantThreads, 0, st>>>(
+        static_cast<uint32_t*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint4*>(x), amax,
+        scale_override, nvecs, cols / 16);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h, int h_rows,
+                 const void* x, uint64_t seed, float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose,
+                 void* stream) {
+  if (int r = check_dims128("rht128_eden", M, N)) return r;
+  Q2B_REQUIRE_PTR(codes);
+  Q2B_REQUIRE_PTR(sf);
+  Q2B_REQUIRE_PTR(scratch);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(ts);
+  Q2B_REQUIRE_NONNULL(scratch_max);
+  if (int r = rht_check_h(h, h_rows)) return r;
+  if (!(fp4_max > 0.f) || !(fp8_max > 0.f)) return fail(Q2B_ERR_INVALID, "fp4_max and fp8_max must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmap;
+  if (int r = make_tmap(&tmap, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 64, 128)) return r;
+  q2b::RhtParams p{};
+  p.M = M;
+  p.N = N;
+  p.h = static_cast<const uint16_t*>(h);
+  p.h_rows = h_rows;
+  p.inv_fp4_max = 1.f / fp4_max;
+  Q2B_CUDA(cudaMemsetAsync(scratch_max, 0, sizeof(unsigned), st));
+  int r;
+  if (transpose) {
+    p.codes_c = static_cast<uint8_t*>(codes);
+    p.scratch_c = static_cast<uint16_t*>(scratch);
+    p.max_c = scratch_max;
+    r = launch_rht<q2b::kInBf16, q2b::kOutCols>(tmap, p, sms, st);
+  } else {
+    p.codes_r = static_cast<uint8_t*>(codes);
+    p.scratch_r = static_cast<uint16_t*>(scratch);
+    p.max_r = scratch_max;
+    r = launch_rht<q2b::kInBf16, q2b::kOutRows>(tmap, p, sms, st);
+  }
+  if (r) return r;
+  return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
+}
+
+int q2b_rht_eden_dual(void* codes_r, void* sf_r, float* ts_r, void* scratch_r, unsigned* max_r, void* codes_c,
+                      void* sf_c, float* ts_c, void* scratch_c, unsigned* max_c, const void* h, int h_rows,
+                      const void* x, uint64_t seed_r, uint64_t seed_c, float fp4_max, float fp8_max, int64_t M,
+                      int64_t N, void* stream) {
+  if (int r = check_dims128("rht128_eden_dual", M, N)) return r;
+  Q2B_REQUIRE_PTR(codes_r);
+  Q2B_REQUIRE_PTR(sf_r);
+  Q2B_REQUIRE_PTR(scratch_r);
+  Q2B_REQUIRE_PTR(codes_c);
+  Q2B_REQUIRE_PTR(sf_c);
+  Q2B_REQUIRE_PTR(scratch_c);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(ts_r);
+  Q2B_REQUIRE_NONNULL(ts_c);
+  Q2B_REQUIRE_NONNULL(max_r);
+  Q2B_REQUIRE_NONNULL(max_c);
+  if (max_r == max_c) return fail(Q2B_ERR_INVALID, "rht128_eden_dual: the two outputs need distinct max words");
+  if (int r = rht_check_h(h, h_rows)) return r;
+  if (!(fp4_max > 0.f) || !(fp8_max > 0.f)) return fail(Q2B_ERR_INVALID, "fp4_max and fp8_max must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmap;
+  if (int r = make_tmap(&tmap, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 64, 128)) return r;
+  q2b::RhtParams p{};
+  p.M = M;
+  p.N = N;
+  p.h = static_cast<const uint16_t*>(h);
+  p.h_rows = h_rows;
+  p.inv_fp4_max = 1.f / fp4_max;
+  p.codes_r = static_cast<uint8_t*>(codes_r);
+  p.scratch_r = static_cast<uint16_t*>(scratch_r);
+  p.max_r = max_r;
+  p.codes_c = static_cast<uint8_t*>(codes_c);
+  p.scratch_c = static_cast<uint16_t*>(scratch_c);
+  p.max_c = max_c;
+  Q2B_CUDA(cudaMemsetAsync(max_r, 0, sizeof(unsigned), st));
+  Q2B_CUDA(cudaMemsetAsync(max_c, 0, sizeof(unsigned), st));
+  if (int r = launch_rht<q2b::kInBf16, q2b::kOutBoth>(tmap, p, sms, st)) return r;
+  if (int r = launch_sr(sf_r, ts_r, scratch_r, max_r, fp8_max, seed_r, M * N / 16, sms, st)) return r;
+  return launch_sr(sf_c, ts_c, scratch_c, max_c, fp8_max, seed_c, M * N / 16, sms, st);
+}
+
+int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h,
+                    int h_rows, const void* x_codes, const void* x_sf, const float* x_ts, uint64_t seed,
+                    float fp4_max, float fp8_max, int64_t M, int64_t N, void* stream) {
+  if (int r = check_dims128("rht128_requant", M, N)) return r;
+  Q2B_REQUIRE_PTR(codes);
+  Q2B_REQUIRE_PTR(sf);
+  Q2B_REQUIRE_PTR(scratch);
+  Q2B_REQUIRE_PTR(x_codes);
+  Q2B_REQUIRE_PTR(x_sf);
+  Q2B_REQUIRE_NONNULL(x_ts);
+  Q2B_REQUIRE_NONNULL(ts);
+  Q2B_REQUIRE_NONNULL(scratch_max);
+  if (int r = rht_check_h(h, h_rows)) return r;
+  if (!(fp4_max > 0.f) || !(fp8_max > 0.f)) return fail(Q2B_ERR_INVALID, "fp4_max and fp8_max must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  q2b::RhtParams p{};
+  p.M = M;
+  p.N = N;
+  p.x_codes = static_cast<const uint8_t*>(x_codes);
+  p.x_sf = static_cast<const uint8_t*>(x_sf);
+  p.x_ts = x_ts;
+  p.h = static_cast<const uint16_t*>(h);
+  p.h_rows = h_rows;
+  p.inv_fp4_max = 1.f / fp4_max;
+  p.codes_c = static_cast<uint8_t*>(codes);
+  p.scratch_c = static_cast<uint16_t*>(scratch);
+  p.max_c = scratch_max;
+  Q2B_CUDA(cudaMemsetAsync(scratch_max, 0, sizeof(unsigned), st));
+  CUtensorMap unused;
+  std::memset(&unused, 0, sizeof(unused));
+  if (int r = launch_rht<q2b::kInFp4, q2b::kOutCols>(unused, p, sms, st)) return r;
+  return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
+}
+
+int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                   int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(Q2B_ERR_INVALID, "fp4_mm: empty problem");
+  if (M % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: M must be divisible by 128 (got %lld)", (long long)M);
+  if (N % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: N must be divisible by 128 (got %lld)", (long long)N);
+  if (K % 64 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: K must be divisible by 64 (got %lld)", (long long)K);
+  Q2B_REQUIRE_PTR(D);
+  Q2B_REQUIRE_PTR(A);
+  Q2B_REQUIRE_PTR(B);
+  Q2B_REQUIRE_PTR(sfa);
+  Q2B_REQUIRE_PTR(sfb);
+  Q2B_REQUIRE_NONNULL(alpha);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb;
+  q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha,
+                    static_cast<__nv_bfloat16*>(D)};
+  if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, 128, 128)) return r;
+  if (N % 256 == 0) {
+    if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 256)) return r;
+    const int64_t tiles = (M / 128) * (N / 256);
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    q2b::gemm_nvfp4_kernel<256><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
+  } else {
+    if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
+    const int64_t tiles = (M / 128) * (N / 128);
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    q2b::gemm_nvfp4_kernel<128><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
+  }
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,389 @@
+// Backward quantizer, pass 1: 128-point rotation on the tensor cores followed
+// by EDEN rounding, for bf16 inputs (the output gradient E) and for NVFP4
+// inputs (requantization of the saved forward operands).
+//
+// Reference semantics (paths relative to the reference project root):
+//   rotation     quartet2/csrc/rht128_eden.cu:10-137 and rht.py:65-82 -- the
+//                effective matrix is swizzle_hadamard(H) built from the 16x128
+//                slice by Sylvester extension (or a full 128x128 matrix for
+//                quant_had_eden, group_transform_and_eden.cu).
+//   EDEN         quartet2/csrc/had128_utils.cuh:155-229 -- per 16 rotated
+//                values: m3 = trunc4(absmax / fp4_max), codes = e2m1_rn(v / m3),
+//                fixed = m3 * sum(w^2) / sum(w * q) kept as bf16, global max of
+//                the bf16 fixed scales by atomicMax.
+//   requant      quartet2/csrc/rht128_requant.cu:79-262 -- codes * e4m3 * ts
+//                rounded to bf16, transposed, rotated along the old rows.
+//
+// B200 design.  A CTA owns one SM and walks 128x128 tiles of the input.
+//   * bf16 input: one TMA warp streams each tile (two 64-column boxes, 128-byte
+//     swizzle) into a 4-stage ring.  NVFP4 input: four producer warps load the
+//     codes and scales with vector loads, dequantize and write the bf16 tile
+//     in the same swizzled layout.
+//   * One MMA warp issues tcgen05.mma kind::f16 M=128 N=128 K=16 x 8 with the
+//     rotation matrix (32 KB, built in shared memory once per CTA) as the B
+//     operand.  The same shared-memory tile serves as a K-major A operand
+//     (rotation along the contiguous dimension: `rows` output) and as an
+//     MN-major A operand (rotation along the row dimension: transposed `cols`
+//     output), so E and E^T are both produced from ONE read of E.
+//   * fp32 results land in TMEM (double-buffered).  Four epilogue warps per
+//     output orientation each own 32 TMEM lanes = 32 output rows; a thread
+//     holds a whole 128-group of its row and runs EDEN with no shuffles,
+//     writing 64 code bytes and eight bf16 scales per group.
+// Scratch scales are written in the blocked 128x4 layout so the scale pass
+// (sr_scales.cuh) is a flat, fully coalesced map.
+#pragma once
+#include <cfloat>
+#include <cuda.h>
+#include "common.cuh"
+
+namespace q2b {
+
+enum RhtInput : int { kInBf16 = 0, kInFp4 = 1 };
+enum RhtOut : int { kOutRows = 1, kOutCols = 2, kOutBoth = 3 };
+
+struct RhtParams {
+  int64_t M, N;                 // input is [M, N] (bf16), or codes [M, N/2] (NVFP4)
+  const uint8_t* x_codes;       // NVFP4 input
+  const uint8_t* x_sf;          //   blocked scales of the input
+  const float* x_ts;            //   input tensor scale
+  const uint16_t* h;            // rotation: 16x128 Sylvester slice or full 128x128 (bf16 bits)
+  int h_rows;                   // 16 or 128
+  uint8_t* codes_r;             // rows output: codes [M, N/2]
+  uint16_t* scratch_r;          //   bf16 fixed scales, blocked [M, N/16]
+  unsigned* max_r;              //   max of the bf16 fixed scales (fp32 bits)
+  uint8_t* codes_c;             // cols output: codes [N, M/2]
+  uint16_t* scratch_c;          //   blocked [N, M/16]
+  unsigned* max_c;
+  float inv_fp4_max;
+};
+
+constexpr int kRhtStages = 4;
+constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one bf16 tile
+constexpr uint32_t kHalfBytes = 128 * 128;      // one 64-column half of a tile
+
+template <int kIn, int kOut>
+struct RhtCfg {
+  static constexpr int kNumOut = (kOut == kOutBoth) ? 2 : 1;
+  static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 4;
+  static constexpr int kMmaWarp = kProdWarps;
+  static constexpr int kEpiWarp0 = kProdWarps + 1;
+  static constexpr int kEpiWarps = 4 * kNumOut;
+  static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
+  static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
+  static constexpr uint32_t kTmemCols = 2 * kColsPerBuf;  // 256 or 512
+  // shared memory: [H 32K][stages x 32K][barriers]
+  static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kRhtStages) + 256;
+};
+
+// Byte offset of bf16 element (r, c) of a 128x128 tile stored as two 64-column
+// halves of 128 rows x 128 bytes with the 128-byte swizzle (16-byte chunk
+// index XOR row % 8).
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+  const int half = c >> 6, q = (c & 63) >> 3;
+  return half * kHalfBytes + r * 128 + (((q ^ (r & 7)) << 4) | ((c & 7) << 1));
+}
+
+// Build the rotation matrix B[p, c] (p = output index, c = input index) in
+// the K-major swizzled layout.
+__device__ __forceinline__ void build_rotation(uint8_t* hs, const uint16_t* h, int h_rows, int tid, int nthreads) {
+  for (int i = tid; i < 128 * 16; i += nthreads) {
+    const int p = i >> 4, q = i & 15;  // q: 16-byte chunk of 8 elements, c = 8q
+    uint4 v;
+    if (h_rows == 16) {
+      const int k = (p >> 6) << 6, l = (p & 63) >> 4, j = p & 15;
+      const int R = k + 4 * l + (j & 3) + 16 * (j >> 2);
+      v = *reinterpret_cast<const uint4*>(h + (R & 15) * 128 + 8 * q);
+      if (__popc((R >> 4) & (q >> 1)) & 1) {
+        v.x ^= 0x80008000u; v.y ^= 0x80008000u; v.z ^= 0x80008000u; v.w ^= 0x80008000u;
+      }
+    } else {
+      v = *reinterpret_cast<const uint4*>(h + p * 128 + 8 * q);
+    }
+    *reinterpret_cast<uint4*>(hs + tile_off(p, 8 * q)) = v;
+  }
+}
+
+// EDEN on 16 rotated values; writes 8 code bytes (as two words) and returns
+// the bf16-rounded fixed scale as fp32.
+__device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, uint32_t& w0, uint32_t& w1,
+                                        uint32_t& fixed_bf16) {
+  float amax = 0.f;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) amax = fmaxf(amax, fabsf(__uint_as_float(r[t])));
+  const float scale = amax * inv_fp4_max;
+  float m3 = __uint_as_float(__float_as_uint(scale) & 0xFFF80000u);
+  float f;
+  if (fabsf(m3) < FLT_MIN) { m3 = 0.f; f = 0.f; } else { f = rcp_rn(m3); }
+  float2 xx = make_float2(0.f, 0.f), xy = make_float2(0.f, 0.f);
+  uint32_t c[2] = {0u, 0u};
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float2 w = fmul2(make_float2(__uint_as_float(r[2 * t]), __uint_as_float(r[2 * t + 1])), make_float2(f, f));
+    const uint32_t b = cvt_e2m1x2(w.x, w.y);
+    const float2 back = f16x2_to_f32x2(e2m1x2_to_f16x2(b));
+    xx = ffma2(w, w, xx);
+    xy = ffma2(w, back, xy);
+    c[t >> 2] |= b << (8 * (t & 3));
+  }
+  const float xx_t = xx.x + xx.y, xy_t = xy.x + xy.y;
+  const float corr = (xy_t == 0.f) ? 1.f : xx_t * rcp_rn(xy_t);
+  const float fixed = m3 * corr;
+  w0 = c[0];
+  w1 = c[1];
+  const uint32_t hb = pack_bf16x2(fixed, 0.f) & 0xFFFFu;
+  fixed_bf16 = hb;
+  return __uint_as_float(hb << 16);
+}
+
+template <int kIn, int kOut>
+__global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
+    rht_eden_kernel(const __grid_constant__ CUtensorMap tmap_x, const RhtParams p) {
+  using Cfg = RhtCfg<kIn, kOut>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* hs = smem;
+  uint8_t* tiles = smem + kTileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + kRhtStages * kTileBytes);
+  uint64_t* empty = full + kRhtStages;
+  uint64_t* tfull = empty + kRhtStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tiles_n = p.N >> 7;
+  const int64_t ntiles = (p.M >> 7) * tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRhtStages; ++s) {
+      mbar_init(&full[s], kIn == kInBf16 ? 1 : 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], Cfg::kEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (kIn == kInBf16 && threadIdx.x == 0) prefetch_tmap(&tmap_x);
+  if (warp == Cfg::kMmaWarp) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  build_rotation(hs, p.h, p.h_rows, threadIdx.x, Cfg::kThreads);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp < Cfg::kProdWarps) {
+    // ------------------------------------------------------------ producer
+    if constexpr (kIn == kInBf16) {
+      if (lane == 0) {
+        const uint64_t policy = policy_evict_first();
+        int it = 0;
+        for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+          const int slot = it % kRhtStages;
+          const uint32_t ph = (it / kRhtStages) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
+          const int tm = static_cast<int>(t / tiles_n), tn = static_cast<int>(t % tiles_n);
+          uint8_t* dst = tiles + slot * kTileBytes;
+          mbar_arrive_expect_tx(&full[slot], kTileBytes);
+          tma_load_2d_hint(dst, &tmap_x, &full[slot], tn * 128, tm * 128, policy);
+          tma_load_2d_hint(dst + kHalfBytes, &tmap_x, &full[slot], tn * 128 + 64, tm * 128, policy);
+        }
+        // drain: make sure no copy is still landing when the CTA retires
+        const int issued = it;
+        for (int k = issued > kRhtStages ? issued - kRhtStages : 0; k < issued; ++k)
+          mbar_wait(&full[k % kRhtStages], (k / kRhtStages) & 1, kTimeoutProducer);
+      }
+    } else {
+      // NVFP4 input: thread r of the 128 producer threads dequantizes row r.
+      const int r = threadIdx.x;  // 0..127
+      const float x_ts = *p.x_ts;
+      const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
+      int it = 0;
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int slot = it % kRhtStages;
+        const uint32_t ph = (it / kRhtStages) & 1;
+        const int64_t tm = t / tiles_n, tn = t % tiles_n;
+        const int64_t row = tm * 128 + r;
+        const uint4* src = reinterpret_cast<const uint4*>(p.x_codes + row * (p.N >> 1) + tn * 64);
+        uint4 q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __ldcs(src + k);
+        const int64_t so = (((row >> 7) * n_kt + (tn * 8 >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2);
+        const uint32_t s_lo = *reinterpret_cast<const uint32_t*>(p.x_sf + so);
+        const uint32_t s_hi = *reinterpret_cast<const uint32_t*>(p.x_sf + so + 512);
+        if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
+        uint8_t* dst = tiles + slot * kTileBytes;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {  // 16-element group g of the row
+          const uint32_t sb = ((g < 4 ? s_lo : s_hi) >> (8 * (g & 3))) & 0xFFu;
+          const float gs = e4m3_to_f32(sb) * x_ts;
+          const uint4 qq = q[g >> 1];
+          const uint32_t w0 = (g & 1) ? qq.z : qq.x, w1 = (g & 1) ? qq.w : qq.y;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {  // 8 elements -> one 16-byte chunk
+            const uint32_t w = hh ? w1 : w0;
+            uint32_t o[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const float2 dq = f16x2_to_f32x2(e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu));
+              const float2 v = fmul2(dq, make_float2(gs, gs));
+              o[b] = pack_bf16x2(v.x, v.y);
+            }
+            *reinterpret_cast<uint4*>(dst + tile_off(r, 16 * g + 8 * hh)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[slot]);
+      }
+    }
+  } else if (warp == Cfg::kMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    const uint32_t id_rows = idesc_bf16(128, 128, false, false);
+    const uint32_t id_cols = idesc_bf16(128, 128, true, false);
+    const uint32_t hs_addr = smem_u32(hs);
+    int it = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+      const int slot = it % kRhtStages;
+      const uint32_t ph = (it / kRhtStages) & 1;
+      const int buf = it & 1;
+      const uint32_t bph = (it >> 1) & 1;
+      ok = mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty) && mbar_wait(&full[slot], ph, kTimeoutTmaFull);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t a_addr = smem_u32(tiles + slot * kTileBytes);
+        const uint32_t d = tmem + buf * Cfg::kColsPerBuf;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint64_t bdesc = smem_desc(hs_addr + (s >> 2) * kHalfBytes + (s & 3) * 32, 0, 1024, kLayoutSW128);
+          if constexpr ((kOut & kOutRows) != 0) {
+            const uint64_t adesc = smem_desc(a_addr + (s >> 2) * kHalfBytes + (s & 3) * 32, 0, 1024, kLayoutSW128);
+            umma_bf16(d, adesc, bdesc, id_rows, s > 0);
+          }
+          if constexpr ((kOut & kOutCols) != 0) {
+            const uint64_t adesc = smem_desc(a_addr + s * 2048, kHalfBytes, 1024, kLayoutSW128);
+            umma_bf16(d + ((kOut & kOutRows) ? 128 : 0), adesc, bdesc, id_cols, s > 0);
+          }
+        }
+        tc_commit(&empty[slot]);
+        tc_commit(&tfull[buf]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
+    const int q = warp & 3;                // TMEM lane quarter this warp may access
+    const int orient = (kOut == kOutBoth) ? (e >> 2) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
+    const uint32_t col_base = (kOut == kOutBoth && orient == 1) ? 128 : 0;
+    uint8_t* codes = orient == 0 ? p.codes_r : p.codes_c;
+    uint16_t* scratch = orient == 0 ? p.scratch_r : p.scratch_c;
+    unsigned* maxp = orient == 0 ? p.max_r : p.max_c;
+    const int64_t out_cols = orient == 0 ? p.N : p.M;  // length of an output row
+    const int64_t n_kblk = out_cols >> 4, n_kt = n_kblk >> 2;
+    float run_max = 0.f;
+    int it = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t bph = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
+      const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
+      uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + ch * 32, r);
+        tmem_ld_wait();
+        if (ch == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+        uint32_t a0, a1, b0, b1, fa, fb;
+        run_max = fmaxf(run_max, eden16(r, p.inv_fp4_max, a0, a1, fa));
+        run_max = fmaxf(run_max, eden16(r + 16, p.inv_fp4_max, b0, b1, fb));
+        __stcs(reinterpret_cast<uint4*>(crow + ch * 16), make_uint4(a0, a1, b0, b1));
+        const int64_t kb = ogrp * 8 + ch * 2;
+        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2) |
+                           (kb & 3);
+        *reinterpret_cast<uint32_t*>(scratch + so) = fa | (fb << 16);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) run_max = fmaxf(run_max, __shfl_xor_sync(0xffffffffu, run_max, o));
+    if (lane == 0) atomicMax(maxp, __float_as_uint(run_max));
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == Cfg::kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// Pass 2: scale of the whole tensor from the global max, then stochastic
+// rounding of every bf16 fixed scale to E4M3 (utils.cuh:336-386,
+// group_transform_and_eden.cu:210-268 of the reference).  Scratch and output
+// are both in the blocked layout; noise for scale i is 16 bits of
+// Philox-4x32-10(key = seed, counter = i / 8).
+__device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint32_t ctr) {
+  uint32_t c0 = ctr, c1 = 0, c2 = 0, c3 = 0;
+  uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return make_uint4(c0, c1, c2, c3);
+}
+
+__device__ __forceinline__ uint32_t sr_e4m3(float in, uint32_t noise16) {
+  const float a = fabsf(in);
+  if (a > 448.f || a < 0.015625f) return cvt_e4m3(in);
+  const uint32_t mask = 0x000FFFFFu;
+  const uint32_t threshold = (noise16 << 4) & mask;
+  uint32_t bits = __float_as_uint(in);
+  bits = ((bits & mask) > threshold) ? (bits | mask) : (bits & ~mask);
+  return cvt_e4m3(__uint_as_float(bits));
+}
+
+__global__ void __launch_bounds__(256) sr_scales_kernel(uint2* __restrict__ sf, float* __restrict__ ts_out,
+                                                        const uint4* __restrict__ scratch,
+                                                        const unsigned* __restrict__ max_bits, float inv_fp8_max,
+                                                        uint64_t seed, int64_t n8) {
+  float gs = __uint_as_float(*max_bits) * inv_fp8_max;
+  float f;
+  if (fabsf(gs) < FLT_MIN) { gs = 0.f; f = 0.f; } else { f = rcp_rn(gs); }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *ts_out = gs;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 s = __ldcs(scratch + i);
+    const uint4 rnd = philox4x32_10(seed, static_cast<uint32_t>(i));
+    const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+    const uint32_t nz[4] = {rnd.x, rnd.y, rnd.z, rnd.w};
+    uint32_t o[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16)) * f;
+      const uint32_t noise = (j & 1) ? (nz[j >> 1] >> 16) : (nz[j >> 1] & 0xFFFFu);
+      o[j >> 2] |= sr_e4m3(v, noise) << (8 * (j & 3));
+    }
+    __stcs(sf + i, make_uint2(o[0], o[1]));
+  }
+}
+
+}  // namespace q2b

@@ -1,0 +1,210 @@
+"""Quartet-II NVFP4 linear layer -- drop-in for ``quartet2.linear`` (reference
+file quartet2/python/quartet2/linear.py; paths are relative to the reference
+project root).
+
+Forward (reference linear.py:155-196): abs-max of input and weight, four-over-
+six (or RNE) NVFP4 quantization of both, NVFP4 GEMM; the NVFP4 operands are
+saved for backward.  Backward (linear.py:200-233): a freshly sign-randomized
+128-point Hadamard rotation, EDEN quantization of the output gradient E and
+of E^T (here from ONE read of E by the dual-orientation kernel), EDEN
+requantization of the saved W^T and X^T, and two NVFP4 GEMMs for dX and dW.
+
+Every kernel is libq2b's (sm_100a CUDA through the C ABI of include/q2b.h);
+the GEMM replaces the reference's flashinfer.mm_fp4(backend="cudnn").
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .quant import (NVFP4QuantMode, abs_max, quant_fp4, rht128_quant_eden, rht128_quant_eden_dual,
+                    rht128_requant)
+
+__all__ = [
+    "Quartet_II_linear", "Quartet_II_fn", "_fp4_mm", "_dq_fp4", "abs_max", "to_blocked", "unblock",
+    "get_hadamard_matrix", "rerotate_hadamard", "register_optimizer_hook",
+]
+
+
+def get_hadamard_matrix(group_size: int, dtype: torch.dtype, device: torch.device):
+    """Sylvester Hadamard matrix scaled by 1/sqrt(n), as the reference builds it
+    from scipy.linalg.hadamard (linear.py:9-15); entries are then rounded to `dtype`."""
+    H = torch.ones(1, 1, dtype=torch.float64)
+    while H.shape[0] < group_size:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
+    if H.shape[0] != group_size:
+        raise ValueError("group_size must be a power of two")
+    return (H * group_size ** -0.5).to(dtype=dtype, device=device).requires_grad_(False)
+
+
+def rerotate_hadamard(hadamard_matrix):
+    """Random +-1 sign per column (the inner dimension of the TN GEMMs), linear.py:25-31."""
+    signs = torch.randint(0, 2, (hadamard_matrix.size(0),), device=hadamard_matrix.device,
+                          dtype=hadamard_matrix.dtype) * 2 - 1
+    return hadamard_matrix * signs[None, :]
+
+
+@torch.library.custom_op("quartet2::fp4_mm", mutates_args=())
+def _fp4_mm(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_mx: torch.Tensor,
+            alpha: torch.Tensor) -> torch.Tensor:
+    """out[m, n] = alpha * dq(x)[m, :] . dq(w)[n, :] in bf16 (reference linear.py:34-56)."""
+    m, packed_k = x_fp4.shape
+    k = packed_k * 2
+    n = w_fp4.shape[0]
+    out = torch.empty([m, n], device=x_fp4.device, dtype=torch.bfloat16)
+    if alpha.dtype != torch.float32:
+        alpha = alpha.float()
+    with torch.cuda.device(x_fp4.device):
+        _lib.call("q2b_gemm_nvfp4", _lib.ptr(out), _lib.ptr(x_fp4), _lib.ptr(w_fp4), _lib.ptr(x_mx),
+                  _lib.ptr(w_mx), _lib.ptr(alpha), m, n, k, _lib.stream_of(x_fp4))
+    return out
+
+
+@_fp4_mm.register_fake
+def _fp4_mm_fake(x_fp4, w_fp4, x_mx, w_mx, alpha):
+    return torch.empty((x_fp4.shape[0], w_fp4.shape[0]), device=x_fp4.device, dtype=torch.bfloat16)
+
+
+def to_blocked(input_matrix) -> torch.Tensor:
+    """[H, W] scale matrix -> flat blocked 128x4 layout (linear.py:64-94)."""
+    rows, cols = input_matrix.shape
+    n_row_blocks = (rows + 127) // 128
+    n_col_blocks = (cols + 3) // 4
+    assert (rows, cols) == (n_row_blocks * 128, n_col_blocks * 4)
+    blocks = input_matrix.view(n_row_blocks, 128, n_col_blocks, 4).permute(0, 2, 1, 3)
+    rearranged = blocks.reshape(-1, 4, 32, 4).transpose(1, 2).reshape(-1, 32, 16)
+    return rearranged.flatten()
+
+
+def unblock(blocked_scales, rows, cols):
+    """Inverse of to_blocked for a [rows, cols/16] scale matrix (linear.py:97-103)."""
+    n_row_blocks, n_col_blocks = rows // 128, (cols // 16) // 4
+    rearranged = blocked_scales.reshape(-1, 32, 4, 4)
+    rearranged = rearranged.permute(0, 2, 1, 3).reshape(-1, n_col_blocks, 128, 4)
+    rearranged = rearranged.permute(0, 2, 1, 3)
+    return rearranged.reshape(n_row_blocks * 128, n_col_blocks * 4)
+
+
+_E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+def _dq_fp4(x_e2m1: torch.Tensor, x_e4m3: torch.Tensor, alpha):
+    """Dequantize NVFP4 codes + blocked scales * alpha to bf16 (linear.py:106-144)."""
+    codes = x_e2m1.view(torch.uint8).to(torch.int32)
+    unpacked = torch.stack([codes & 0xF, (codes >> 4) & 0xF], dim=-1).flatten(start_dim=-2)
+    grid = torch.tensor(_E2M1, dtype=torch.float32, device=x_e2m1.device)
+    vals = grid[unpacked]
+    scales = unblock(x_e4m3.to(torch.float32), x_e2m1.shape[0], x_e2m1.shape[1] * 2)
+    out = (vals.unflatten(dim=-1, sizes=(-1, 16)) * scales[..., None]).flatten(start_dim=-2) * alpha
+    return out.to(torch.bfloat16)
+
+
+class Quartet_II_fn(torch.autograd.Function):
+    group_size = 16
+
+    @staticmethod
+    def forward(ctx, input, weight, had, mode: NVFP4QuantMode, disable_backward_quant: bool = False,
+                weight_amax: torch.Tensor = None, input_amax: torch.Tensor = None,
+                scratch_amax: torch.Tensor = None):
+        ctx.batch = input.shape[0]
+        ctx.seq = input.shape[1]
+        ctx.in_dim = weight.shape[1]
+        ctx.out_dim = weight.shape[0]
+        ctx.disable_backward_quant = disable_backward_quant
+        ctx.scratch_amax = scratch_amax
+        ctx.had = had
+
+        if torch.is_autocast_enabled("cuda"):
+            input = input.to(torch.bfloat16)
+            weight = weight.to(torch.bfloat16)
+        elif weight.dtype != torch.bfloat16:
+            raise TypeError("Weight must be bfloat16. Either set `dtype=torch.bfloat16` or enable autocast`")
+        elif input.dtype != torch.bfloat16:
+            raise TypeError("Input must be bfloat16. Either cast input to bfloat16 or enable autocast`")
+
+        forward_scale_override = 1.0
+        flat_input = input.reshape(-1, input.shape[-1]).contiguous()
+        weight = weight.contiguous()
+        if input_amax is None:
+            input_amax = abs_max(flat_input)
+        if weight_amax is None:
+            weight_amax = abs_max(weight)
+        input_fp4 = quant_fp4(flat_input, amax=input_amax, scale_override=forward_scale_override, mode=mode)
+        weight_fp4 = quant_fp4(weight, amax=weight_amax, scale_override=forward_scale_override, mode=mode)
+        ctx.save_for_backward(input_fp4.fp4, input_fp4.micro_scales, input_fp4.tensor_scale,
+                              weight_fp4.fp4, weight_fp4.micro_scales, weight_fp4.tensor_scale)
+        res = _fp4_mm(input_fp4.fp4, weight_fp4.fp4, input_fp4.micro_scales, weight_fp4.micro_scales,
+                      alpha=input_fp4.tensor_scale * weight_fp4.tensor_scale)
+        return res.reshape(ctx.batch, ctx.seq, ctx.out_dim)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        xfp4, xs, xm, wfp4, ws, wm = ctx.saved_tensors
+        backward_scale_override = (17 / 16) * 0.93
+        if torch.is_autocast_enabled("cuda"):
+            grad_output = grad_output.to(torch.bfloat16)
+        had = rerotate_hadamard(ctx.had)
+        flat_grad_output = grad_output.reshape(-1, grad_output.shape[-1]).contiguous()
+
+        if ctx.disable_backward_quant:
+            xr = _dq_fp4(xfp4, xs, xm)
+            wr = _dq_fp4(wfp4, ws, wm)
+            grad_input = flat_grad_output @ wr
+            grad_weight = flat_grad_output.T @ xr
+            return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
+
+        h16 = had[:16, :].contiguous()
+        # E and E^T from one pass over the output gradient
+        e_q, et_q = rht128_quant_eden_dual(h=h16, x=flat_grad_output, scale_override=backward_scale_override,
+                                           scratch_amax=ctx.scratch_amax)
+        wt_q = rht128_requant(x=wfp4, x_group_scales=ws, x_tensor_scale=wm, h=h16,
+                              scale_override=backward_scale_override, scratch_amax=ctx.scratch_amax)
+        grad_input = _fp4_mm(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
+                             alpha=e_q.tensor_scale * wt_q.tensor_scale)
+        xt_q = rht128_requant(x=xfp4, x_group_scales=xs, x_tensor_scale=xm, h=h16,
+                              scale_override=backward_scale_override, scratch_amax=ctx.scratch_amax)
+        grad_weight = _fp4_mm(et_q.fp4, xt_q.fp4, et_q.micro_scales, xt_q.micro_scales,
+                              alpha=et_q.tensor_scale * xt_q.tensor_scale)
+        return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
+
+
+class Quartet_II_linear(torch.nn.Linear):
+    """nn.Linear whose forward/backward run the Quartet-II NVFP4 recipe.
+
+    As in the reference (linear.py:236-256) the bias parameter exists but is
+    not added by forward."""
+
+    def __init__(self, *args, four_over_six=True, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.mode = NVFP4QuantMode.FOUR_SIX if four_over_six else NVFP4QuantMode.RNE
+        self.weight_abs_max = None
+        had = get_hadamard_matrix(128, torch.bfloat16, self.weight.device) if self.weight.device.type != "meta" else None
+        self.register_buffer("had", had, persistent=False)
+        self.register_buffer("scratch_amax", torch.empty((), dtype=torch.uint32, device=self.weight.device),
+                             persistent=False)
+
+    def _apply(self, fn):
+        old_device = self.weight.device
+        super()._apply(fn)
+        if old_device.type == "meta" and self.weight.device.type != "meta":
+            self.had = get_hadamard_matrix(128, torch.bfloat16, self.weight.device)
+        return self
+
+    def forward(self, x, disable_backward_quant=False, input_abs_max=None):
+        return Quartet_II_fn.apply(x, self.weight[...], self.had, self.mode, disable_backward_quant,
+                                   self.weight_abs_max, input_abs_max, self.scratch_amax)
+
+
+def register_optimizer_hook(model: torch.nn.Module, optimizer: torch.optim.Optimizer):
+    """After every optimizer step cache each Quartet layer's weight abs-max (linear.py:259-270)."""
+    opt_params = {id(p) for group in optimizer.param_groups for p in group["params"]}
+    quartet_modules = [m for m in model.modules() if isinstance(m, Quartet_II_linear) and id(m.weight) in opt_params]
+
+    def hook(opt, args, kwargs):
+        for m in quartet_modules:
+            w = m.weight.detach()
+            if w.dtype != torch.bfloat16:
+                w = w.to(torch.bfloat16)
+            m.weight_abs_max = abs_max(w)
+
+    return optimizer.register_step_post_hook(hook)

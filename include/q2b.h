@@ -1,0 +1,105 @@
+/*
+ * q2b.h -- C ABI of libq2b, the B200 (sm_100a) implementation of the
+ * Quartet-II NVFP4 linear-layer hot path of IST-DASLab/CloverLM.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t (as
+ * void*), launches asynchronously on that stream, allocates no device memory
+ * and returns Q2B_OK or an error code; q2b_last_error() then describes the
+ * failure (thread-local).  Callers own every buffer, including scratch.
+ *
+ * Layouts (shared with the reference):
+ *   bf16 tensors      row-major, 16-byte aligned.
+ *   E2M1 codes        uint8 [rows, cols/2]; the low nibble holds the even element.
+ *   E4M3 scales       one byte per 16 elements along a row, stored in the
+ *                     blocked 128x4 layout: offset of (row r, block k) with
+ *                     n = cols/16 blocks per row is
+ *                     ((r/128 * n/4 + k/4) << 9) | (r%32)<<4 | ((r/32)%4)<<2 | k%4
+ *                     (reference quartet2/csrc/utils.cuh:392-410).
+ *   tensor scale      one fp32 in device memory; value = code * scale * ts.
+ * Shape rules: rows and cols multiples of 128 (reference quant.py:117-121).
+ * Paths in comments are relative to the reference project root.
+ */
+#ifndef Q2B_H
+#define Q2B_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  Q2B_OK = 0,
+  Q2B_ERR_INVALID = 1, /* bad shape, null or misaligned pointer, bad mode */
+  Q2B_ERR_CUDA = 2,    /* a CUDA runtime/driver call failed */
+  Q2B_ERR_DEVICE = 3   /* current device is not an sm_100 (B200-class) GPU */
+};
+
+enum { Q2B_MODE_RNE = 0, Q2B_MODE_FOUR_SIX = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int q2b_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* q2b_last_error(void);
+
+/* Reads and clears the device-side watchdog word of the current device: 0 if
+ * no kernel wait ever timed out, else the code of the first wait that gave up.
+ * Synchronizes the device. */
+int q2b_device_status(unsigned* code);
+
+/* out[0] = max |x| over n bf16 values (fp32).
+ * Replaces: abs_max (torch.compile reduction), quartet2/python/quartet2/linear.py:146-148. */
+int q2b_abs_max(float* out, const void* x, int64_t n, void* stream);
+
+/* Forward RTN quantization of bf16 x [rows, cols] to NVFP4 with tensor scale
+ * from *amax; mode Q2B_MODE_RNE or Q2B_MODE_FOUR_SIX.
+ * Replaces: rtn_fp4 / four_six_fp4, quartet2/csrc/round_four_six.cu:125-153
+ * (bound in quartet2/csrc/binding.cpp, used by quant.py:114-138). */
+int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                  int64_t rows, int64_t cols, int mode, void* stream);
+
+/* Rotation by the 128-point randomized Hadamard transform (h: h_rows = 16,
+ * the top slice, extended by Sylvester's construction and row-swizzled as
+ * quartet2/python/quartet2/rht.py:65-82) or by an explicit 128x128 matrix
+ * (h_rows = 128), then EDEN quantization with a stochastically rounded E4M3
+ * scale (seed keys the noise).  x is bf16 [M, N]; transpose = 0 quantizes
+ * rows (codes [M, N/2]), transpose = 1 quantizes x^T (codes [N, M/2]).
+ * scratch: bf16 [M*N/16]; scratch_max: one uint32.
+ * Replaces: transform_rht128_eden, quartet2/csrc/rht128_eden.cu:171-177, and
+ * group_transform_128_eden, quartet2/csrc/group_transform_and_eden.cu:321-329. */
+int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h, int h_rows,
+                 const void* x, uint64_t seed, float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose,
+                 void* stream);
+
+/* Both orientations of q2b_rht_eden from one read of x: the row output uses
+ * (codes_r, sf_r, ts_r, scratch_r, max_r, seed_r), the transposed output
+ * (codes_c, ..., seed_c).  Equal, element for element, to two q2b_rht_eden
+ * calls with transpose = 0 and 1.
+ * Replaces: the two rht128_quant_eden calls on the output gradient in
+ * Quartet_II_fn.backward, quartet2/python/quartet2/linear.py:222,229. */
+int q2b_rht_eden_dual(void* codes_r, void* sf_r, float* ts_r, void* scratch_r, unsigned* max_r, void* codes_c,
+                      void* sf_c, float* ts_c, void* scratch_c, unsigned* max_c, const void* h, int h_rows,
+                      const void* x, uint64_t seed_r, uint64_t seed_c, float fp4_max, float fp8_max, int64_t M,
+                      int64_t N, void* stream);
+
+/* Requantization of an NVFP4 tensor (codes [M, N/2], blocked scales, tensor
+ * scale *x_ts): dequantize to bf16, transpose, rotate along the old rows,
+ * EDEN.  Output codes [N, M/2], scales blocked [N, M/16].
+ * Replaces: rht128_requant, quartet2/csrc/rht128_requant.cu:303-311. */
+int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h,
+                    int h_rows, const void* x_codes, const void* x_sf, const float* x_ts, uint64_t seed,
+                    float fp4_max, float fp8_max, int64_t M, int64_t N, void* stream);
+
+/* D[M, N] (bf16) = *alpha * dequant(A[M, K]) @ dequant(B[N, K])^T for NVFP4
+ * operands (codes K-major, blocked scales).  M, N multiples of 128, K of 64.
+ * Replaces: _fp4_mm -> flashinfer.mm_fp4(..., backend="cudnn"),
+ * quartet2/python/quartet2/linear.py:34-56. */
+int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                   int64_t M, int64_t N, int64_t K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q2B_H */

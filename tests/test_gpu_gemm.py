@@ -1,0 +1,96 @@
+"""GPU parity of the tcgen05 NVFP4 GEMM: within 1e-2 relative Frobenius error
+of an fp32 matmul of the dequantized operands (the bar BASELINE.json sets)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from cloverlm_b200 import _lib
+from cloverlm_b200.linear import _dq_fp4, _fp4_mm
+from cloverlm_b200.quant import NVFP4QuantMode, quant_fp4
+from helpers import u8
+
+pytestmark = pytest.mark.gpu
+
+REL_FRO_TOL = 1e-2
+
+
+@pytest.fixture(autouse=True)
+def _no_watchdog():
+    yield
+    assert _lib.device_status() == 0, "a kernel wait timed out"
+
+
+def _blocky(rows, cols, seed):
+    """Values whose magnitude varies by 2^[-6, 6] per (row, 16-block): a scale
+    factor applied to the wrong row or block shows up as a large error."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, cols, generator=g)
+    e = torch.randint(-6, 7, (rows, cols // 16), generator=g).float()
+    x = x * torch.exp2(e).repeat_interleave(16, dim=1)
+    return x.to(torch.bfloat16).cuda()
+
+
+def _dq(q):
+    return _dq_fp4(q.fp4, q.micro_scales, 1.0).float() * q.tensor_scale.float()
+
+
+def _dq_exact(q):
+    """fp32 dequantization without bf16 rounding (oracle)."""
+    return torch.from_numpy(oracle.dequant(u8(q.fp4), u8(q.micro_scales).reshape(-1), q.tensor_scale.item())).cuda()
+
+
+def _check(M, N, K, seed, blocky=False):
+    mk = _blocky if blocky else (lambda r, c, s: torch.randn(r, c, generator=torch.Generator().manual_seed(s))
+                                 .to(torch.bfloat16).cuda())
+    a = mk(M, K, seed)
+    b = mk(N, K, seed + 1)
+    qa = quant_fp4(a, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    qb = quant_fp4(b, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    out = _fp4_mm(qa.fp4, qb.fp4, qa.micro_scales, qb.micro_scales, qa.tensor_scale * qb.tensor_scale)
+    assert out.dtype == torch.bfloat16 and out.shape == (M, N)
+    ref = _dq_exact(qa) @ _dq_exact(qb).T
+    rel = ((out.float() - ref).norm() / ref.norm()).item()
+    assert rel <= REL_FRO_TOL, rel
+    return rel
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (128, 256, 256), (256, 384, 384), (128, 128, 640),
+                                   (384, 512, 1024), (1024, 3584, 3584), (256, 896, 3584)])
+def test_gemm_random(M, N, K):
+    rel = _check(M, N, K, seed=M + N + K)
+    assert rel < 5e-3  # bf16 output rounding dominates
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (512, 256, 768), (256, 128, 1152)])
+def test_gemm_blocky_scales(M, N, K):
+    _check(M, N, K, seed=7, blocky=True)
+
+
+def test_gemm_large_k_wgrad_shape():
+    # wgrad-like: long contraction (tokens), small output
+    _check(512, 512, 16384, seed=3)
+
+
+def test_gemm_exact_small_integers():
+    """Codes with unit scales and ts=1 make the product exact in fp32."""
+    M, N, K = 256, 256, 512
+    g = torch.Generator().manual_seed(0)
+    ca = torch.randint(0, 256, (M, K // 2), generator=g, dtype=torch.uint8)
+    cb = torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8)
+    # scale byte 0x38 = 1.0 in E4M3
+    sa = torch.full((M * K // 16,), 0x38, dtype=torch.uint8)
+    sb = torch.full((N * K // 16,), 0x38, dtype=torch.uint8)
+    one = torch.ones((), device="cuda")
+    out = _fp4_mm(ca.cuda(), cb.cuda(), sa.view(torch.float8_e4m3fn).cuda(), sb.view(torch.float8_e4m3fn).cuda(), one)
+    A = torch.from_numpy(oracle.dequant(ca.numpy(), sa.numpy(), 1.0)).double()
+    B = torch.from_numpy(oracle.dequant(cb.numpy(), sb.numpy(), 1.0)).double()
+    ref = (A @ B.T).to(torch.bfloat16)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_gemm_rejects_bad_shapes():
+    a = torch.zeros(128, 40, dtype=torch.uint8, device="cuda")
+    s = torch.zeros(128 * 5, dtype=torch.uint8, device="cuda").view(torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="K must be divisible by 64"):
+        _fp4_mm(a, a, s, s, torch.ones((), device="cuda"))

@@ -1,0 +1,213 @@
+"""GPU parity of the quantizer kernels against the CPU oracle (C restatement
+of the reference kernels).  Everything goes through libq2b's C ABI."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from cloverlm_b200 import _lib
+from cloverlm_b200.linear import get_hadamard_matrix, rerotate_hadamard
+from cloverlm_b200.quant import (NVFP4QuantMode, abs_max, quant_fp4, quant_had_eden, rht128_quant_eden,
+                                 rht128_quant_eden_dual, rht128_requant)
+from cloverlm_b200.rht import swizzle_hadamard
+from helpers import bf16_bits, randn_bf16, student_t_bf16, u8
+
+pytestmark = pytest.mark.gpu
+
+BWD_SO = (17 / 16) * 0.93
+# Rotations are summed by the tensor cores in an implementation-defined order;
+# the oracle rounds the exact sum once.  Code/scale bytes may differ only where
+# a value sits on a rounding boundary.
+TIE_FRACTION = 1e-4
+
+SHAPES = [(128, 128), (256, 128), (128, 1024), (1024, 640), (512, 3584)]
+
+
+@pytest.fixture(autouse=True)
+def _no_watchdog():
+    yield
+    assert _lib.device_status() == 0, "a kernel wait timed out"
+
+
+def _mismatch(a: np.ndarray, b: np.ndarray) -> float:
+    return float((a.reshape(-1) != b.reshape(-1)).mean())
+
+
+@pytest.mark.parametrize("shape", SHAPES + [(2048, 3584)])
+def test_abs_max_exact(shape):
+    x = randn_bf16(*shape, seed=3, outliers=1e-3, device="cuda")
+    got = abs_max(x).item()
+    assert got == oracle.amax(bf16_bits(x))
+    assert got == x.float().abs().max().item()
+
+
+@pytest.mark.parametrize("mode", [NVFP4QuantMode.RNE, NVFP4QuantMode.FOUR_SIX])
+@pytest.mark.parametrize("shape", SHAPES + [(2048, 3584)])
+def test_quant_fwd_bit_exact(mode, shape):
+    x = randn_bf16(*shape, seed=11, outliers=1e-3, device="cuda")
+    q, s, t = quant_fp4(x, scale_override=1.0, mode=mode)
+    codes, sf, ts = oracle.quant_fp4(bf16_bits(x), scale_override=1.0, four_six=(mode == NVFP4QuantMode.FOUR_SIX))
+    assert t.item() == np.float32(ts)
+    np.testing.assert_array_equal(u8(q), codes)
+    np.testing.assert_array_equal(u8(s).reshape(-1), sf)
+
+
+@pytest.mark.parametrize("mode", [NVFP4QuantMode.RNE, NVFP4QuantMode.FOUR_SIX])
+@pytest.mark.parametrize("so", [1.0, 0.9])
+def test_quant_fwd_student_t_and_override(mode, so):
+    x = student_t_bf16(1024, 3584, seed=1, device="cuda")
+    q, s, t = quant_fp4(x, scale_override=so, mode=mode)
+    codes, sf, ts = oracle.quant_fp4(bf16_bits(x), scale_override=so, four_six=(mode == NVFP4QuantMode.FOUR_SIX))
+    assert t.item() == np.float32(ts)
+    np.testing.assert_array_equal(u8(q), codes)
+    np.testing.assert_array_equal(u8(s).reshape(-1), sf)
+
+
+def test_quant_fwd_edge_values():
+    """Zeros, fully underflowing groups (stored scale byte 0), huge and tiny values."""
+    x = torch.zeros(256, 256, dtype=torch.bfloat16, device="cuda")
+    x[0, :16] = 1e-30
+    x[1, :] = 3e38
+    x[2, 5] = -7.0
+    x[3, :] = torch.linspace(-5, 5, 256)
+    for mode in (NVFP4QuantMode.RNE, NVFP4QuantMode.FOUR_SIX):
+        amax = torch.tensor(3e38, device="cuda")
+        q, s, t = quant_fp4(x, scale_override=1.0, amax=amax.float(), mode=mode)
+        codes, sf, ts = oracle.quant_fp4(bf16_bits(x), amax_value=3e38, four_six=(mode == NVFP4QuantMode.FOUR_SIX))
+        np.testing.assert_array_equal(u8(q), codes)
+        np.testing.assert_array_equal(u8(s).reshape(-1), sf)
+    # all-zero tensor: tensor scale 1
+    z = torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda")
+    q, s, t = quant_fp4(z, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    assert t.item() == 1.0 and int(u8(q).max()) == 0 and int(u8(s).max()) == 0
+
+
+def _h16(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    h = get_hadamard_matrix(128, torch.bfloat16, "cpu")
+    signs = (torch.randint(0, 2, (128,), generator=g) * 2 - 1).to(torch.bfloat16)
+    return (h * signs[None, :]).contiguous()
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("shape", SHAPES + [(2048, 3584)])
+def test_rht128_eden_vs_oracle(shape, transpose):
+    x = randn_bf16(*shape, seed=21, device="cuda")
+    H = _h16(1)
+    h16 = H[:16].contiguous()
+    q, s, t = rht128_quant_eden(h=h16.cuda(), x=x, seed=torch.tensor(42), scale_override=BWD_SO, transpose=transpose)
+    codes, sf, ts = oracle.rht128_quant_eden(bf16_bits(x), bf16_bits(h16), seed=42, scale_override=BWD_SO,
+                                             transpose=transpose)
+    assert t.item() == np.float32(ts)
+    assert _mismatch(u8(q), codes) <= TIE_FRACTION
+    assert _mismatch(u8(s).reshape(-1), sf) <= TIE_FRACTION
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_quant_had_eden_full_matrix_vs_oracle(transpose):
+    x = student_t_bf16(512, 1024, seed=5, device="cuda")
+    g = torch.Generator().manual_seed(7)
+    H = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    q, s, t = quant_had_eden(h=H.cuda(), x=x, seed=torch.tensor(9), transpose=transpose)
+    codes, sf, ts = oracle.quant_had_eden(bf16_bits(x), bf16_bits(H), seed=9, transpose=transpose)
+    assert t.item() == np.float32(ts)
+    assert _mismatch(u8(q), codes) <= TIE_FRACTION
+    assert _mismatch(u8(s).reshape(-1), sf) <= TIE_FRACTION
+
+
+@pytest.mark.parametrize("shape", [(128, 128), (1024, 640), (2048, 3584)])
+def test_rht16_equals_full_swizzled(shape):
+    """Reference test_rht.py:49-59 on the GPU: the 16-row slice path equals the
+    explicit swizzled matrix path, bit for bit."""
+    x = randn_bf16(*shape, seed=4, device="cuda")
+    H = (_h16(3).float() * 128 ** 0.5).to(torch.bfloat16).cuda()  # unnormalized +-1 entries
+    for transpose in (False, True):
+        rq, rs, rg = quant_had_eden(x=x, h=swizzle_hadamard(H), transpose=transpose, seed=torch.tensor(42))
+        tq, ts, tg = rht128_quant_eden(h=H[:16].contiguous(), x=x, transpose=transpose, seed=torch.tensor(42))
+        assert rg.item() == tg.item()
+        assert torch.equal(rs.view(torch.uint8), ts.view(torch.uint8))
+        assert torch.equal(rq, tq)
+
+
+@pytest.mark.parametrize("shape", [(128, 256), (1024, 640), (2048, 3584)])
+def test_dual_equals_two_single_calls(shape):
+    x = randn_bf16(*shape, seed=8, device="cuda")
+    h16 = _h16(2)[:16].contiguous().cuda()
+    a, at = rht128_quant_eden_dual(h=h16, x=x, seed=torch.tensor(5), seed_t=torch.tensor(6), scale_override=BWD_SO)
+    b = rht128_quant_eden(h=h16, x=x, seed=torch.tensor(5), scale_override=BWD_SO)
+    bt = rht128_quant_eden(h=h16, x=x, seed=torch.tensor(6), scale_override=BWD_SO, transpose=True)
+    for u, v in ((a, b), (at, bt)):
+        assert torch.equal(u.fp4, v.fp4)
+        assert torch.equal(u.micro_scales.view(torch.uint8), v.micro_scales.view(torch.uint8))
+        assert u.tensor_scale.item() == v.tensor_scale.item()
+
+
+@pytest.mark.parametrize("shape", [(128, 128), (256, 512), (1024, 640), (2048, 3584)])
+def test_requant_vs_oracle(shape):
+    x = randn_bf16(*shape, seed=31, outliers=1e-3, device="cuda")
+    q, s, t = quant_fp4(x, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    h16 = _h16(4)[:16].contiguous()
+    rq, rs, rt = rht128_requant(x=q, x_group_scales=s, x_tensor_scale=t, h=h16.cuda(), seed=torch.tensor(77),
+                                scale_override=BWD_SO)
+    codes, sf, ts = oracle.rht128_requant(u8(q), u8(s).reshape(-1), t.item(), bf16_bits(h16), seed=77,
+                                          scale_override=BWD_SO)
+    assert rq.shape == (shape[1], shape[0] // 2)
+    assert rt.item() == np.float32(ts)
+    assert _mismatch(u8(rq), codes) <= TIE_FRACTION
+    assert _mismatch(u8(rs).reshape(-1), sf) <= TIE_FRACTION
+
+
+def test_eden_effective_bitwidth_floors():
+    """Reference test_rounding.py:95-133 floors, measured on our kernels."""
+    x = torch.randn(4096, 2048, device="cuda", dtype=torch.bfloat16)
+    xf = x.float().cpu().numpy()
+    for mode, floor in ((NVFP4QuantMode.RNE, 3.38), (NVFP4QuantMode.FOUR_SIX, 3.52),
+                        (NVFP4QuantMode.EDEN, 3.32)):
+        q, s, t = quant_fp4(x, scale_override=1.0, mode=mode, seed=torch.tensor(42))
+        dq = oracle.dequant(u8(q), u8(s).reshape(-1), t.item())
+        err = ((xf - dq) ** 2).sum(-1) / (xf ** 2).sum(-1)
+        assert -np.log2(err.mean()) / 2 > floor, mode
+    H = get_hadamard_matrix(128, torch.bfloat16, "cuda")
+    for transpose in (False, True):
+        q, s, t = rht128_quant_eden(h=H[:16].contiguous(), x=x, transpose=transpose)
+        ref = oracle.rotate(bf16_bits(x), bf16_bits(swizzle_hadamard(H)), transpose)
+        dq = oracle.dequant(u8(q), u8(s).reshape(-1), t.item())
+        err = ((ref - dq) ** 2).sum(-1) / (ref ** 2).sum(-1)
+        assert -np.log2(err.mean()) / 2 > 3.2
+
+
+def test_sr_scales_unbiased():
+    """Mean-unbiasedness of the stochastic scale rounding: averaging the
+    dequantized scales over many seeds converges to the exact bf16 scale."""
+    x = randn_bf16(256, 1024, seed=12, device="cuda")
+    h16 = _h16(5)[:16].contiguous().cuda()
+    _, scratch, mb = oracle.eden_pass1(oracle.rotate(bf16_bits(x), oracle.rht_matrix_from_slice(bf16_bits(h16.cpu()))),
+                                       1.0)
+    exact = oracle.bf16_to_f32(scratch)  # [rows, cols/16], natural order
+    table = oracle.e4m3_table()
+    acc = np.zeros_like(exact, dtype=np.float64)
+    n = 256
+    for i in range(n):
+        q, s, t = rht128_quant_eden(h=h16, x=x, seed=torch.tensor(1000 + i))
+        sf = oracle.unblock(u8(s).reshape(-1), exact.shape[0], exact.shape[1])
+        acc += table[sf] * t.item()
+    mean = acc / n
+    rel = np.abs(mean - exact).sum() / np.abs(exact).sum()
+    # E4M3 spacing is 1/8 relative; RN would leave a bias of ~2-3%; SR averages down ~1/sqrt(n)
+    assert rel < 4e-3, rel
+    q, s, t = rht128_quant_eden(h=h16, x=x, seed=torch.tensor(1))
+    rn = oracle.unblock(u8(s).reshape(-1), exact.shape[0], exact.shape[1])
+    assert (table[rn] * t.item() != exact).mean() > 0.5  # individual draws are not RN copies
+
+
+def test_errors_match_reference_messages():
+    x = torch.zeros(100, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(AssertionError):
+        quant_fp4(x, scale_override=1.0)
+    from cloverlm_b200.quant import _rtn_fp4_op
+    o = torch.empty(128, 32, dtype=torch.uint8, device="cuda")
+    s = torch.empty(128 * 4, dtype=torch.uint8, device="cuda")
+    t = torch.empty((), device="cuda")
+    x = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="cols must be divisible by 128"):
+        _rtn_fp4_op(o, s, t, x, torch.ones((), device="cuda"), 1.0)
