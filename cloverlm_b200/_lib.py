@@ -34,6 +34,7 @@ SIGNATURES = {
     "q2b_abs_max": [_P, _P, _I64, _P],
     "q2b_quant_fwd": [_P, _P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_rht_eden": [_P, _P, _P, _P, _P, _P, _INT, _P, _U64, _F, _F, _I64, _I64, _INT, _P],
+    "q2b_rht_eden_noalloc": [_P, _P, _P, _P, _INT, _P, _U64, _F, _F, _I64, _I64, _INT, _P],
     "q2b_rht_eden_dual": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _P, _U64, _U64, _F, _F, _I64, _I64, _P],
     "q2b_rht_requant": [_P, _P, _P, _P, _P, _P, _INT, _P, _P, _P, _U64, _F, _F, _I64, _I64, _P],
     "q2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],

@@ -270,6 +270,79 @@ int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scra
   return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free q2b_rht_eden.  Its scratch (bf16 pre-rounding scales, then
+// the uint32 max word at the end) is this file-scope device array; host code
+// must not pass the symbol itself to a kernel -- on the host it names a
+// stand-in, not device memory -- but the address cudaGetSymbolAddress returns
+// for the current device.
+}  // extern "C"
+
+namespace {
+static __device__ __align__(256) unsigned char g_noalloc_scratch[Q2B_NOALLOC_SCRATCH_BYTES + 256];
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    Q2B_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (p == nullptr) return fail(Q2B_ERR_CUDA, "cudaGetSymbolAddress returned a null scratch address");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = static_cast<unsigned char*>(g_noalloc_addr[dev]);
+  return Q2B_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int q2b_rht_eden_noalloc(void* codes, void* sf, float* ts, const void* h, int h_rows, const void* x, uint64_t seed,
+                         float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose, void* stream) {
+  if (int r = check_dims128("rht128_eden_noalloc", M, N)) return r;
+  if (M * N > Q2B_NOALLOC_MAX_ELEMS)
+    return fail(Q2B_ERR_INVALID,
+                "rht128_eden_noalloc: M*N = %lld exceeds the static scratch limit of %lld elements "
+                "(use q2b_rht_eden with caller-provided scratch)",
+                static_cast<long long>(M * N), static_cast<long long>(Q2B_NOALLOC_MAX_ELEMS));
+  Q2B_REQUIRE_PTR(codes);
+  Q2B_REQUIRE_PTR(sf);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(ts);
+  if (int r = rht_check_h(h, h_rows)) return r;
+  if (!(fp4_max > 0.f) || !(fp8_max > 0.f)) return fail(Q2B_ERR_INVALID, "fp4_max and fp8_max must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  unsigned char* scratch = nullptr;
+  if (int r = noalloc_scratch(dev, &scratch)) return r;
+  unsigned* scratch_max = reinterpret_cast<unsigned*>(scratch + Q2B_NOALLOC_SCRATCH_BYTES);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmap;
+  if (int r = make_tmap(&tmap, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 64, 128)) return r;
+  q2b::RhtParams p{};
+  p.M = M;
+  p.N = N;
+  p.h = static_cast<const uint16_t*>(h);
+  p.h_rows = h_rows;
+  p.inv_fp4_max = 1.f / fp4_max;
+  Q2B_CUDA(cudaMemsetAsync(scratch_max, 0, sizeof(unsigned), st));
+  int r;
+  if (transpose) {
+    p.codes_c = static_cast<uint8_t*>(codes);
+    p.scratch_c = reinterpret_cast<uint16_t*>(scratch);
+    p.max_c = scratch_max;
+    r = launch_rht<q2b::kInBf16, q2b::kOutCols>(tmap, p, sms, st);
+  } else {
+    p.codes_r = static_cast<uint8_t*>(codes);
+    p.scratch_r = reinterpret_cast<uint16_t*>(scratch);
+    p.max_r = scratch_max;
+    r = launch_rht<q2b::kInBf16, q2b::kOutRows>(tmap, p, sms, st);
+  }
+  if (r) return r;
+  return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
+}
+
 int q2b_rht_eden_dual(void* codes_r, void* sf_r, float* ts_r, void* scratch_r, unsigned* max_r, void* codes_c,
                       void* sf_c, float* ts_c, void* scratch_c, unsigned* max_c, const void* h, int h_rows,
                       const void* x, uint64_t seed_r, uint64_t seed_c, float fp4_max, float fp8_max, int64_t M,

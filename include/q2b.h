@@ -72,6 +72,31 @@ int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scra
                  const void* x, uint64_t seed, float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose,
                  void* stream);
 
+/* Allocation-free variant of q2b_rht_eden.  No counterpart in the reference.
+ *
+ * For callers that may not allocate device memory at all -- for example code
+ * running inside a host framework that owns every device byte through its own
+ * pool and hands an operator only its input and output buffers, or a
+ * latency-critical path where cudaMalloc's implicit device synchronization is
+ * not acceptable -- this entry point needs no scratch from the caller.  The
+ * bf16 pre-rounding scales and the max word live in one static device buffer
+ * inside libq2b (Q2B_NOALLOC_SCRATCH_BYTES plus 256 bytes, held on every GPU
+ * that loads the library until the process exits).  Inputs and outputs are as
+ * for q2b_rht_eden.
+ *
+ * Limit: M * N <= Q2B_NOALLOC_MAX_ELEMS (one bf16 scale per 16 elements);
+ * larger inputs are rejected with Q2B_ERR_INVALID.
+ * The first call on a device looks up the buffer's device address (once per
+ * device, under a lock); make that first call before any stream capture.
+ * All calls share the one buffer: calls whose kernels overlap on the GPU
+ * (different streams, or different host threads, without ordering) race and
+ * produce wrong results -- serialize them.  The max word is cleared on every
+ * call; the scale area is fully overwritten before it is read. */
+#define Q2B_NOALLOC_SCRATCH_BYTES (16ll << 20)
+#define Q2B_NOALLOC_MAX_ELEMS (Q2B_NOALLOC_SCRATCH_BYTES * 8)
+int q2b_rht_eden_noalloc(void* codes, void* sf, float* ts, const void* h, int h_rows, const void* x, uint64_t seed,
+                         float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose, void* stream);
+
 /* Both orientations of q2b_rht_eden from one read of x: the row output uses
  * (codes_r, sf_r, ts_r, scratch_r, max_r, seed_r), the transposed output
  * (codes_c, ..., seed_c).  Equal, element for element, to two q2b_rht_eden
