@@ -44,14 +44,29 @@ struct GemmCfg {
   static constexpr uint32_t kSfaBytes = 4 * 512;
   static constexpr uint32_t kSfbBytes = (BN / 128) * 4 * 512;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr uint32_t kSfaCol = 256;        // TMEM column of the A scales (16 cols)
-  static constexpr uint32_t kSfbCol = 272;        // B scales (16 or 32 cols)
+  // TMEM: accumulators in [0, 256); one scale-factor column set per stage
+  // after them (A: 4 K steps x 4 columns, B: 4 K steps x BN/32 columns).
+  static constexpr uint32_t kSfSetCols = 16 + 4 * (BN / 32);
+  static constexpr uint32_t kSfBase = 256;
   static constexpr uint32_t kTmemCols = 512;
+  static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
   static constexpr int kEpiWarps = 8;
-  static constexpr int kThreads = 32 * (2 + kEpiWarps);
-  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr int kEpiWarp0 = 3;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
 };
 
+// Warp roles:
+//   0  TMA producer      (waits empty[s], loads A/B/scales, arrives full[s])
+//   1  MMA issuer        (waits sfready[s], 4 x tcgen05.mma, commits empty[s])
+//   2  scale-copy issuer (waits full[s], tcgen05.cp of the stage's scales into
+//                         TMEM column set s, commits sfready[s])
+//   3+ epilogue
+// The scale copies run on their own warp because tcgen05.cp and tcgen05.mma
+// issued by one thread serialize with each other in this pipeline, while
+// copies issued by a second warp overlap the MMAs of earlier stages.  Column
+// set s is free again when full[s] fires, because the producer reloads stage
+// s only after the MMAs that read set s have completed (empty[s]).
 template <int BN>
 __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -61,20 +76,23 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
   uint64_t* empty = full + Cfg::kStages;
-  uint64_t* tfull = empty + Cfg::kStages;
+  uint64_t* sfready = empty + Cfg::kStages;
+  uint64_t* tfull = sfready + Cfg::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tiles_m = p.M / Cfg::BM, tiles_n = p.N / BN;
-  const int64_t ntiles = tiles_m * tiles_n;
+  const int64_t tiles_n = p.N / BN;
+  const int64_t ntiles = (p.M / Cfg::BM) * tiles_n;
   const int64_t nkb = (p.K + 255) / 256;
   const int64_t n_kt = p.K / 64;  // 64-element scale chunks along K
+  const int tail_nk = static_cast<int>((p.K % 256) / 64);  // K steps in a partial last block (0 = none)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sfready[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -92,6 +110,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  const uint32_t smem_base = smem_u32(smem);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -104,7 +123,10 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           const int slot = static_cast<int>(it % Cfg::kStages);
           const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
-          const int nk = static_cast<int>((p.K - kb * 256) / 64 < 4 ? (p.K - kb * 256) / 64 : 4);
+#ifdef Q2B_GEMM_PROBE_NO_TMA
+          if (true) { mbar_arrive(&full[slot]); continue; }
+#endif
+          const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
           uint8_t* st = smem + slot * Cfg::kStageBytes;
           const uint32_t sf_bytes = nk * 512u;
           mbar_arrive_expect_tx(&full[slot], Cfg::kABytes + Cfg::kBBytes + sf_bytes * (1 + BN / 128));
@@ -122,9 +144,39 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
         mbar_wait(&full[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ scale copies
+    // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
+    const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
+    const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
+    int64_t it = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+        const int slot = static_cast<int>(it % Cfg::kStages);
+        const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+        if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+          const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+          const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+          for (int j = 0; j < nk; ++j) {
+            tmem_cp_32x128b_x4(set + 4 * j, sfa_d0 + so + 32 * j);
+#pragma unroll
+            for (int u = 0; u < BN / 128; ++u)
+              tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
+          }
+          tc_commit(&sfready[slot]);
+        }
+        __syncwarp();
+      }
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
     const uint32_t idesc = idesc_nvf4(Cfg::BM, BN);
+    const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
+    const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
     int64_t it = 0, tc = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
@@ -136,25 +188,20 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
         const int slot = static_cast<int>(it % Cfg::kStages);
         const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-        if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+        if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
-          const int nk = static_cast<int>((p.K - kb * 256) / 64 < 4 ? (p.K - kb * 256) / 64 : 4);
-          const uint32_t st = smem_u32(smem + slot * Cfg::kStageBytes);
-          const uint32_t sfa_s = st + Cfg::kABytes + Cfg::kBBytes;
-          const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
-          for (int j = 0; j < nk; ++j) {
-            tmem_cp_32x128b_x4(tmem + Cfg::kSfaCol + 4 * j, smem_desc(sfa_s + 512 * j, 0, 128, kLayoutNone));
+          const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+          const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+          if (kb == nkb - 1 && tail_nk) {
+            for (int j = 0; j < tail_nk; ++j)
+              umma_nvf4(d, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
+                        (kb > 0 || j > 0) ? 1u : 0u);
+          } else {
 #pragma unroll
-            for (int u = 0; u < BN / 128; ++u)
-              tmem_cp_32x128b_x4(tmem + Cfg::kSfbCol + (BN / 32) * j + 4 * u,
-                                 smem_desc(sfb_s + u * 2048 + 512 * j, 0, 128, kLayoutNone));
-          }
-          for (int j = 0; j < nk; ++j) {
-            const uint64_t adesc = smem_desc(st + 32 * j, 0, 1024, kLayoutSW128);
-            const uint64_t bdesc = smem_desc(st + Cfg::kABytes + 32 * j, 0, 1024, kLayoutSW128);
-            umma_nvf4(d, adesc, bdesc, idesc, tmem + Cfg::kSfaCol + 4 * j, tmem + Cfg::kSfbCol + (BN / 32) * j,
-                      (kb > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < 4; ++j)
+              umma_nvf4(d, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
+                        (kb > 0 || j > 0) ? 1u : 0u);
           }
           tc_commit(&empty[slot]);
         }
@@ -166,7 +213,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int e = warp - 2;
+    const int e = warp - Cfg::kEpiWarp0;
     const int q = warp & 3;  // TMEM lane quarter
     constexpr int kColsPerWarp = BN / 2;
     const int c0 = (e >> 2) * kColsPerWarp;
@@ -181,20 +228,23 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       const int64_t row = tm * Cfg::BM + q * 32 + lane;
       __nv_bfloat16* drow = p.D + row * p.N + tn * BN + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + c0;
-#pragma unroll 1
-      for (int ch = 0; ch < kColsPerWarp / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + ch * 32, r);
-        tmem_ld_wait();
-        if (ch == kColsPerWarp / 32 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-        }
+      // Drain the whole accumulator slice into registers first and hand the
+      // TMEM buffer back to the MMA warp at once; the bf16 conversion and the
+      // global stores then overlap the next tile's MMAs.
+      constexpr int kChunks = kColsPerWarp / 32;
+      uint32_t r[kChunks][32];
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) {
         uint32_t o[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          o[k] = pack_bf16x2(__uint_as_float(r[2 * k]) * alpha, __uint_as_float(r[2 * k + 1]) * alpha);
+          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
         uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
 #pragma unroll
         for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
@@ -208,6 +258,246 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+}
+
+}  // namespace q2b
+
+namespace q2b {
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs (an SM pair) computes a 256x256 output
+// tile with tcgen05.mma.cta_group::2 (M=256 across the pair, N=256).  Each CTA
+// loads its own 128 rows of A and its own 128-row half of B, so per SM a K
+// block needs 16 + 16 KB of operands instead of 16 + 32 KB, and five stages
+// fit.  Scale factors: each CTA holds the A scales of its rows and the B
+// scales of all 256 columns (four-way lane-replicated, as tcgen05.cp 32x128b
+// .warpx4 writes them); one 2-CTA copy instruction fills both CTAs' TMEM.
+//   leader (rank 0): TMA warp, MMA warp, epilogue; its full[] barriers count
+//                    the bytes of BOTH CTAs (.cta_group::2 TMA completes on
+//                    the leader's barrier), its tempty[] collects both CTAs'
+//                    epilogue warps.
+//   peer   (rank 1): TMA warp and epilogue.
+// Every wait is bounded; both CTAs meet at a cluster barrier before TMEM is
+// freed and before exit, so no CTA leaves while its peer can still touch its
+// shared memory or TMEM.
+struct Gemm2Cfg {
+  static constexpr int kStages = 5;
+  static constexpr uint32_t kABytes = 128 * 128;            // this CTA's 128 rows x 128 B of K
+  static constexpr uint32_t kBBytes = 128 * 128;            // this CTA's half of B
+  static constexpr uint32_t kSfaBytes = 2048;               // 4 chunks (one per K=64 step) of 128 rows
+  static constexpr uint32_t kSfbBytes = 4096;               // 2 x 128 rows x 4 chunks
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 38 KB
+  static constexpr uint32_t kSfSetCols = 48, kSfBase = 256, kTmemCols = 512;
+  static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kEpiWarp0 = 3;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
+};
+
+// Arrive on the leader CTA's copy of `bar` when this thread's prior 2-CTA
+// tcgen05 ops complete.
+__device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 1;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Warp roles (both CTAs unless noted):
+//   0  TMA producer; its loads complete on the LEADER's full[s]
+//   1  MMA issuer (leader): waits sfready[s], cta_group::2 MMAs, multicast-commits empty[s]
+//   2  scale-copy issuer (leader): waits full[s], cta_group::2 tcgen05.cp into set s, commits sfready[s]
+//   3+ epilogue: drains its own TMEM rows, arrives on the leader's tempty
+__global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
+    gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                          const GemmParams p) {
+  using Cfg = Gemm2Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* sfready = empty + Cfg::kStages;
+  uint64_t* tfull = sfready + Cfg::kStages;
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int64_t tiles_n = p.N / 256;
+  const int64_t ntiles = (p.M / 256) * tiles_n;
+  const int64_t nkb = (p.K + 255) / 256;
+  const int64_t n_kt = p.K / 64;
+  const int tail_nk = static_cast<int>((p.K % 256) / 64);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&sfready[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 2 * Cfg::kEpiWarps);
+    fence_barrier_init();
+  }
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
+  }
+  cluster_sync();  // both CTAs resident, barriers initialized
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int64_t it = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
+        const int64_t tm = t / tiles_n, tn = t % tiles_n;
+        const int a_row = static_cast<int>(tm * 256 + rank * 128);
+        const int b_row = static_cast<int>(tn * 256 + rank * 128);
+        const int64_t sfa_chunk0 = (tm * 2 + rank) * n_kt;
+        const int64_t sfb_chunk0 = (tn * 2) * n_kt;
+        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+          const int slot = static_cast<int>(it % Cfg::kStages);
+          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+          uint8_t* st = smem + slot * Cfg::kStageBytes;
+          const uint32_t bar = map_to_rank(smem_u32(&full[slot]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(st, &tmap_a, bar, static_cast<int>(kb * 128), a_row);
+          tma_load_2d_pair(st + Cfg::kABytes, &tmap_b, bar, static_cast<int>(kb * 128), b_row);
+          // scale chunks: 512 B each, viewed as rows of 256 B
+          tma_load_2d_pair(st + Cfg::kABytes + Cfg::kBBytes, &tmap_sfa, bar, 0,
+                           static_cast<int>((sfa_chunk0 + kb * 4) * 2));
+          tma_load_2d_pair(st + Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes, &tmap_sfb, bar, 0,
+                           static_cast<int>((sfb_chunk0 + kb * 4) * 2));
+          tma_load_2d_pair(st + Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + 2048, &tmap_sfb, bar, 0,
+                           static_cast<int>((sfb_chunk0 + n_kt + kb * 4) * 2));
+        }
+      }
+      // drain: every issued stage is released by the MMAs (or the watchdog tripped)
+      const int64_t issued = it;
+      for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
+        mbar_wait(&empty[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ scale copies (leader)
+    if (leader) {
+      const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
+      const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
+      int64_t it = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
+        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+          const int slot = static_cast<int>(it % Cfg::kStages);
+          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+          if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
+          if (lane == 0) {
+            const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+            const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+            const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+            for (int j = 0; j < nk; ++j) {
+              tmem_cp_32x128b_x4_pair(set + 4 * j, sfa_d0 + so + 32 * j);
+              tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + so + 32 * j);
+              tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + so + 128 + 32 * j);
+            }
+            tc_commit_pair_leader(&sfready[slot]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue (leader)
+    if (leader) {
+      const uint32_t idesc = idesc_nvf4(256, 256);
+      const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
+      const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
+      int64_t it = 0, tc = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters, ++tc) {
+        const uint32_t bph = static_cast<uint32_t>(tc) & 1;
+        if (!mbar_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+          const int slot = static_cast<int>(it % Cfg::kStages);
+          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+          if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+            const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+            const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+            for (int j = 0; j < nk; ++j)
+              umma_nvf4_pair(tmem, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
+                             (kb > 0 || j > 0) ? 1u : 0u);
+            tc_commit_pair(&empty[slot]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) tc_commit_pair(tfull);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int e = warp - Cfg::kEpiWarp0;
+    const int q = warp & 3;
+    const int c0 = (e >> 2) * 128;
+    const float alpha = *p.alpha;
+    const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
+    int64_t tc = 0;
+    for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
+      if (!mbar_wait(tfull, static_cast<uint32_t>(tc) & 1, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      const int64_t row = tm * 256 + rank * 128 + q * 32 + lane;
+      __nv_bfloat16* drow = p.D + row * p.N + tn * 256 + c0;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
+      uint32_t r[4][32];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t o[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
+        uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+  }
+  cluster_sync();
 }
 
 }  // namespace q2b

@@ -98,6 +98,7 @@ int device_setup(int* dev_out, int* sms_out) {
     Q2B_CUDA(set_smem(rht_eden_kernel<kInFp4, kOutCols>, RhtCfg<kInFp4, kOutCols>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256>, GemmCfg<256>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128>, GemmCfg<128>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel, Gemm2Cfg::kSmemBytes));
     d.ready = true;
   }
   *dev_out = dev;
@@ -108,13 +109,14 @@ int device_setup(int* dev_out, int* sms_out) {
 // 2-D tensor map over a row-major [rows, inner] matrix with a box of
 // box_inner x box_rows elements and the 128-byte swizzle.
 int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
-              uint64_t rows, uint32_t box_inner, uint32_t box_rows) {
+              uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {inner * elem_bytes};
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(Q2B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return Q2B_OK;
@@ -441,7 +443,40 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
   q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha,
                     static_cast<__nv_bfloat16*>(D)};
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, 128, 128)) return r;
+#ifdef Q2B_GEMM_USE_2SM
+  if (M % 256 == 0 && N % 256 == 0 && sms >= 2) {
+    // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair
+    CUtensorMap tsa, tsb;
+    if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
+    if (int r = make_tmap(&tsa, sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, M * K / 16 / 256, 256, 8,
+                          CU_TENSOR_MAP_SWIZZLE_NONE))
+      return r;
+    if (int r = make_tmap(&tsb, sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, N * K / 16 / 256, 256, 8,
+                          CU_TENSOR_MAP_SWIZZLE_NONE))
+      return r;
+    const int64_t tiles = (M / 256) * (N / 256);
+    const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+    cfg.blockDim = dim3(q2b::Gemm2Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = q2b::Gemm2Cfg::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel, ta, tb, tsa, tsb, p));
+    return Q2B_OK;
+  }
+#endif
+#ifdef Q2B_GEMM_PROBE_BN128
+  if (false) {
+#else
   if (N % 256 == 0) {
+#endif
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 256)) return r;
     const int64_t tiles = (M / 128) * (N / 256);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);

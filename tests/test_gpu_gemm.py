@@ -56,7 +56,9 @@ def _check(M, N, K, seed, blocky=False):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (128, 256, 256), (256, 384, 384), (128, 128, 640),
-                                   (384, 512, 1024), (1024, 3584, 3584), (256, 896, 3584)])
+                                   (384, 512, 1024), (1024, 3584, 3584), (256, 896, 3584),
+                                   # 256x256-divisible shapes take the 2-SM (cta_group::2) kernel
+                                   (256, 256, 128), (512, 768, 384), (768, 512, 640), (2048, 2048, 2048)])
 def test_gemm_random(M, N, K):
     rel = _check(M, N, K, seed=M + N + K)
     assert rel < 5e-3  # bf16 output rounding dominates
