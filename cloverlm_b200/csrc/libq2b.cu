@@ -216,18 +216,23 @@ int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* 
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t nvecs = rows * cols / 8;
-  const int64_t per_block = int64_t(q2b::kQuantThreads) * q2b::kQuantUnroll;
-  const int64_t want = (nvecs + per_block - 1) / per_block;
+  const int64_t ngroups = rows * cols / 16;
+  if (ngroups >= (int64_t(1) << 32)) return fail(Q2B_ERR_INVALID, "%s: tensor too large", name);
+  if ((reinterpret_cast<uintptr_t>(x) & 31u) != 0)
+    return fail(Q2B_ERR_INVALID, "Pointer `x` is not aligned to 32 bytes");
+  const uint32_t gpr = static_cast<uint32_t>(cols / 16);
+  // ceil(2^64 / gpr): floor(g * magic / 2^64) == g / gpr exactly for every 32-bit g
+  const uint64_t magic = ~uint64_t(0) / gpr + 1;
+  const int64_t want = (ngroups + 255) / 256;
   const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
   if (mode == Q2B_MODE_FOUR_SIX)
-    q2b::quant_fwd_kernel<true><<<blocks, q2b::kQuantThreads, 0, st>>>(
-        static_cast<uint32_t*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint4*>(x), amax,
-        scale_override, nvecs, cols / 16);
+    q2b::quant_fwd_v2_kernel<true><<<blocks, 256, 0, st>>>(
+        static_cast<uint2*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint16_t*>(x), amax,
+        scale_override, static_cast<uint32_t>(ngroups), gpr, magic);
   else
-    q2b::quant_fwd_kernel<false><<<blocks, q2b::kQuantThreads, 0, st>>>(
-        static_cast<uint32_t*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint4*>(x), amax,
-        scale_override, nvecs, cols / 16);
+    q2b::quant_fwd_v2_kernel<false><<<blocks, 256, 0, st>>>(
+        static_cast<uint2*>(codes), static_cast<uint8_t*>(sf), ts, static_cast<const uint16_t*>(x), amax,
+        scale_override, static_cast<uint32_t>(ngroups), gpr, magic);
   Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
 }

@@ -8,19 +8,15 @@
 // candidate with the strictly lower squared error is kept (a tie keeps 6).
 // Reciprocals are IEEE-rounded (the reference uses rcp.approx).
 //
-// Work decomposition: one thread per 8 consecutive bf16 (one 16-byte load);
-// lane pairs (2j, 2j+1) hold one 16-element group.  A warp covers 256
-// consecutive elements, so its loads and code stores are fully coalesced;
-// lane 8q gathers the four scale bytes of its k-tile with shuffles and writes
-// them as one 32-bit word of the blocked layout.  Every thread keeps kUnroll
-// independent 16-byte loads in flight.
+// Work decomposition: one thread per 16-element group (one 32-byte load), a
+// warp covers 512 consecutive elements, so its loads and 8-byte code stores
+// are fully coalesced; lane 4q gathers the four scale bytes of its k-tile with
+// shuffles and writes them as one 32-bit word of the blocked layout.
 #pragma once
 #include "common.cuh"
 
 namespace q2b {
 
-constexpr int kQuantThreads = 256;
-constexpr int kQuantUnroll = 4;
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -42,39 +38,51 @@ __device__ __forceinline__ void fill_quant_tables(QuantTables& t, float ts) {
   }
 }
 
-// Quantize my 8 values with one candidate; returns the group's squared error
-// (both lanes of the pair get the same value).
-__device__ __forceinline__ float quant_candidate(const float (&x)[8], float gabs, float inv_val_so, float inv_ts,
-                                                 const QuantTables& tab, uint32_t& codes, uint32_t& s8) {
-  const float s_group = gabs * inv_val_so;
-  s8 = cvt_e4m3(s_group * inv_ts);
+// ---------------------------------------------------------------------------
+// v2: one thread per 16-element group (a 32-byte load), so the group's
+// abs-max and squared errors need no shuffles; row/column of the group come
+// from a 64-bit multiply-high by a precomputed reciprocal instead of a
+// division.  Errors are accumulated on magnitudes: d = |x| - |q| * descale
+// is, bit for bit, the negation of x - q * descale whenever x < 0 (q has the
+// sign of x and rounding is symmetric), so d*d is unchanged.
+__device__ __forceinline__ void ldg256(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ float quant16(const float (&xs)[16], const float (&xa)[16], float gabs, float inv_c,
+                                         float inv_ts, const QuantTables& tab, uint2& codes, uint32_t& s8) {
+  s8 = cvt_e4m3(gabs * inv_c * inv_ts);
   const float f = tab.factor[s8];
-  codes = 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float2 w = fmul2(make_float2(x[2 * k], x[2 * k + 1]), make_float2(f, f));
-    codes |= cvt_e2m1x2(w.x, w.y) << (8 * k);
-  }
   const float nd = -tab.descale[s8];
-  float2 sum = make_float2(0.f, 0.f);
+  uint32_t b[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 w = fmul2(make_float2(xs[2 * k], xs[2 * k + 1]), make_float2(f, f));
+    b[k] = cvt_e2m1x2(w.x, w.y);
+  }
+  codes.x = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
+  codes.y = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
+  float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    float2 dq = f16x2_to_f32x2(e2m1x2_to_f16x2((codes >> (8 * k)) & 0xFFu));
-    float2 d = ffma2(dq, make_float2(nd, nd), make_float2(x[2 * k], x[2 * k + 1]));
-    sum = ffma2(d, d, sum);
+    const float2 q0 = f16x2_to_f32x2(e2m1x2_to_f16x2(b[k] & 0x77u));
+    const float2 d0 = ffma2(q0, make_float2(nd, nd), make_float2(xa[2 * k], xa[2 * k + 1]));
+    s0 = ffma2(d0, d0, s0);
+    const float2 q1 = f16x2_to_f32x2(e2m1x2_to_f16x2(b[4 + k] & 0x77u));
+    const float2 d1 = ffma2(q1, make_float2(nd, nd), make_float2(xa[8 + 2 * k], xa[8 + 2 * k + 1]));
+    s1 = ffma2(d1, d1, s1);
   }
-  const float local = sum.x + sum.y;
-  return local + __shfl_xor_sync(0xffffffffu, local, 1);
+  return (s0.x + s0.y) + (s1.x + s1.y);
 }
 
 template <bool kFourSix>
-__global__ void __launch_bounds__(kQuantThreads) quant_fwd_kernel(uint32_t* __restrict__ codes,
-                                                                  uint8_t* __restrict__ sf,
-                                                                  float* __restrict__ ts_out,
-                                                                  const uint4* __restrict__ x,
-                                                                  const float* __restrict__ amax_ptr,
-                                                                  float scale_override, int64_t nvecs,
-                                                                  int64_t groups_per_row) {
+__global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ codes, uint8_t* __restrict__ sf,
+                                                           float* __restrict__ ts_out,
+                                                           const uint16_t* __restrict__ x,
+                                                           const float* __restrict__ amax_ptr, float scale_override,
+                                                           uint32_t ngroups, uint32_t gpr, uint64_t gpr_magic) {
   __shared__ QuantTables tab;
   const float amax = *amax_ptr;
   const float inv_scales_max = kFourSix ? 1.f / 256.f : 1.f / 448.f;
@@ -89,48 +97,41 @@ __global__ void __launch_bounds__(kQuantThreads) quant_fwd_kernel(uint32_t* __re
   const float inv6 = (1.f / 6.f) * scale_override;
   const float inv4 = (1.f / 4.f) * scale_override;
   const int lane = threadIdx.x & 31;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t n_ktiles = groups_per_row >> 2;
-
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < nvecs;
-       base += stride * kQuantUnroll) {
-    uint4 v[kQuantUnroll];
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t n_kt = gpr >> 2;
+  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
+    uint32_t w[8];
+    ldg256(x + static_cast<uint64_t>(g) * 16, w);
+    float xs[16], xa[16];
+    float gabs = 0.f;
 #pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t idx = base + u * stride;
-      if (idx < nvecs) v[u] = __ldcs(x + idx);
+    for (int k = 0; k < 8; ++k) {
+      xs[2 * k] = bf16lo(w[k]);
+      xs[2 * k + 1] = bf16hi(w[k]);
+      const uint32_t a = w[k] & 0x7FFF7FFFu;
+      xa[2 * k] = bf16lo(a);
+      xa[2 * k + 1] = bf16hi(a);
+      gabs = fmaxf(gabs, fmaxf(xa[2 * k], xa[2 * k + 1]));
     }
-#pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t idx = base + u * stride;
-      if (idx >= nvecs) break;  // warp-uniform: nvecs is a multiple of 32
-      float xv[8] = {bf16lo(v[u].x), bf16hi(v[u].x), bf16lo(v[u].y), bf16hi(v[u].y),
-                     bf16lo(v[u].z), bf16hi(v[u].z), bf16lo(v[u].w), bf16hi(v[u].w)};
-      float a = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(xv[k]));
-      const float gabs = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-
-      uint32_t c6, s6;
-      const float e6 = quant_candidate(xv, gabs, inv6, inv_ts, tab, c6, s6);
-      uint32_t c = c6, s = s6;
-      if constexpr (kFourSix) {
-        uint32_t c4, s4;
-        const float e4 = quant_candidate(xv, gabs, inv4, inv_ts, tab, c4, s4);
-        if (e4 < e6) { c = c4; s = s4; }
-      }
-      __stcs(codes + idx, c);
-      // gather the scale bytes of groups 4q..4q+3 (lanes 8q, 8q+2, 8q+4, 8q+6)
-      const uint32_t b1 = __shfl_down_sync(0xffffffffu, s, 2);
-      const uint32_t b2 = __shfl_down_sync(0xffffffffu, s, 4);
-      const uint32_t b3 = __shfl_down_sync(0xffffffffu, s, 6);
-      if ((lane & 7) == 0) {
-        const int64_t grp = idx >> 1;
-        const int64_t row = grp / groups_per_row;
-        const int64_t kb = grp - row * groups_per_row;
-        const int64_t off = (((row >> 7) * n_ktiles + (kb >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2);
-        *reinterpret_cast<uint32_t*>(sf + off) = s | (b1 << 8) | (b2 << 16) | (b3 << 24);
-      }
+    uint2 c;
+    uint32_t s;
+    const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, s);
+    if constexpr (kFourSix) {
+      uint2 c4;
+      uint32_t s4;
+      const float e4 = quant16(xs, xa, gabs, inv4, inv_ts, tab, c4, s4);
+      if (e4 < e6) { c = c4; s = s4; }
+    }
+    __stcs(codes + g, c);
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, s, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, s, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, s, 3);
+    if ((lane & 3) == 0) {
+      const uint32_t row = static_cast<uint32_t>(__umul64hi(static_cast<uint64_t>(g), gpr_magic));
+      const uint32_t kb = g - row * gpr;
+      const uint64_t off = ((static_cast<uint64_t>(row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) |
+                           (((row >> 5) & 3) << 2);
+      *reinterpret_cast<uint32_t*>(sf + off) = s | (b1 << 8) | (b2 << 16) | (b3 << 24);
     }
   }
 }

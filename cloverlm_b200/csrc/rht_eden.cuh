@@ -25,10 +25,11 @@
 //     (rotation along the contiguous dimension: `rows` output) and as an
 //     MN-major A operand (rotation along the row dimension: transposed `cols`
 //     output), so E and E^T are both produced from ONE read of E.
-//   * fp32 results land in TMEM (double-buffered).  Four epilogue warps per
-//     output orientation each own 32 TMEM lanes = 32 output rows; a thread
-//     holds a whole 128-group of its row and runs EDEN with no shuffles,
-//     writing 64 code bytes and eight bf16 scales per group.
+//   * fp32 results land in TMEM (double-buffered).  Eight epilogue warps per
+//     output orientation: two per TMEM lane quarter (32 output rows), each
+//     taking 64 of the 128 rotated values; a thread runs EDEN on four whole
+//     16-groups of its row with no shuffles, writing 32 code bytes and four
+//     bf16 scales.
 // Scratch scales are written in the blocked 128x4 layout so the scale pass
 // (sr_scales.cuh) is a flat, fully coalesced map.
 #pragma once
@@ -64,10 +65,11 @@ constexpr uint32_t kHalfBytes = 128 * 128;      // one 64-column half of a tile
 template <int kIn, int kOut>
 struct RhtCfg {
   static constexpr int kNumOut = (kOut == kOutBoth) ? 2 : 1;
-  static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 4;
+  static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 8;
   static constexpr int kMmaWarp = kProdWarps;
   static constexpr int kEpiWarp0 = kProdWarps + 1;
-  static constexpr int kEpiWarps = 4 * kNumOut;
+  // two warps per TMEM lane quarter and output orientation, 64 columns each
+  static constexpr int kEpiWarps = 8 * kNumOut;
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
   static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
   static constexpr uint32_t kTmemCols = 2 * kColsPerBuf;  // 256 or 512
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRhtStages; ++s) {
-      mbar_init(&full[s], kIn == kInBf16 ? 1 : 128);
+      mbar_init(&full[s], kIn == kInBf16 ? 1 : 32 * Cfg::kProdWarps);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -198,34 +200,42 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           mbar_wait(&full[k % kRhtStages], (k / kRhtStages) & 1, kTimeoutProducer);
       }
     } else {
-      // NVFP4 input: thread r of the 128 producer threads dequantizes row r.
-      const int r = threadIdx.x;  // 0..127
+      // NVFP4 input: each producer thread dequantizes whole 16-element groups
+      // of the tile (8 code bytes + 1 scale byte -> 32 bytes of bf16); eight
+      // consecutive lanes cover one row's 64-byte code segment, so a warp's
+      // loads are contiguous 64-byte runs.
+      const int pt = threadIdx.x;  // 0 .. 32*kProdWarps-1
       const float x_ts = *p.x_ts;
       const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
+      constexpr int kItems = 128 * 8 / (32 * Cfg::kProdWarps);  // (row, 16-col group) items per thread
       int it = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int slot = it % kRhtStages;
         const uint32_t ph = (it / kRhtStages) & 1;
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
-        const int64_t row = tm * 128 + r;
-        const uint4* src = reinterpret_cast<const uint4*>(p.x_codes + row * (p.N >> 1) + tn * 64);
-        uint4 q[4];
+        uint2 q[kItems];
+        uint32_t sb[kItems];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = __ldcs(src + k);
-        const int64_t so = (((row >> 7) * n_kt + (tn * 8 >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2);
-        const uint32_t s_lo = *reinterpret_cast<const uint32_t*>(p.x_sf + so);
-        const uint32_t s_hi = *reinterpret_cast<const uint32_t*>(p.x_sf + so + 512);
+        for (int u = 0; u < kItems; ++u) {
+          const int item = pt + u * 32 * Cfg::kProdWarps;
+          const int r = item >> 3, g = item & 7;  // row, 16-col group of the tile
+          const int64_t row = tm * 128 + r;
+          q[u] = __ldcs(reinterpret_cast<const uint2*>(p.x_codes + row * (p.N >> 1) + tn * 64 + g * 8));
+          const int64_t kb = tn * 8 + g;
+          const int64_t so = (((row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2) |
+                             (kb & 3);
+          sb[u] = p.x_sf[so];
+        }
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
         uint8_t* dst = tiles + slot * kTileBytes;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {  // 16-element group g of the row
-          const uint32_t sb = ((g < 4 ? s_lo : s_hi) >> (8 * (g & 3))) & 0xFFu;
-          const float gs = e4m3_to_f32(sb) * x_ts;
-          const uint4 qq = q[g >> 1];
-          const uint32_t w0 = (g & 1) ? qq.z : qq.x, w1 = (g & 1) ? qq.w : qq.y;
+        for (int u = 0; u < kItems; ++u) {
+          const int item = pt + u * 32 * Cfg::kProdWarps;
+          const int r = item >> 3, g = item & 7;
+          const float gs = e4m3_to_f32(sb[u]) * x_ts;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {  // 8 elements -> one 16-byte chunk
-            const uint32_t w = hh ? w1 : w0;
+          for (int half = 0; half < 2; ++half) {  // 8 elements -> one 16-byte chunk
+            const uint32_t w = half ? q[u].y : q[u].x;
             uint32_t o[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
@@ -233,7 +243,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
               const float2 v = fmul2(dq, make_float2(gs, gs));
               o[b] = pack_bf16x2(v.x, v.y);
             }
-            *reinterpret_cast<uint4*>(dst + tile_off(r, 16 * g + 8 * hh)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + tile_off(r, 16 * g + 8 * half)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_proxy_async_smem();
@@ -279,8 +289,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
     const int q = warp & 3;                // TMEM lane quarter this warp may access
-    const int orient = (kOut == kOutBoth) ? (e >> 2) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
-    const uint32_t col_base = (kOut == kOutBoth && orient == 1) ? 128 : 0;
+    const int orient = (kOut == kOutBoth) ? (e >> 3) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
+    const int colhalf = (e >> 2) & 1;      // which 64 of the group's 128 outputs
+    const uint32_t col_base = ((kOut == kOutBoth && orient == 1) ? 128 : 0) + colhalf * 64;
     uint8_t* codes = orient == 0 ? p.codes_r : p.codes_c;
     uint16_t* scratch = orient == 0 ? p.scratch_r : p.scratch_c;
     unsigned* maxp = orient == 0 ? p.max_r : p.max_c;
@@ -296,27 +307,24 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
       const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
       const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
-      uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64;
+      uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + colhalf * 32;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + ch * 32, r);
-        tmem_ld_wait();
-        if (ch == 3) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-        }
-        uint32_t a0, a1, b0, b1, fa, fb;
-        run_max = fmaxf(run_max, eden16(r, p.inv_fp4_max, a0, a1, fa));
-        run_max = fmaxf(run_max, eden16(r + 16, p.inv_fp4_max, b0, b1, fb));
-        __stcs(reinterpret_cast<uint4*>(crow + ch * 16), make_uint4(a0, a1, b0, b1));
-        const int64_t kb = ogrp * 8 + ch * 2;
-        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2) |
-                           (kb & 3);
-        *reinterpret_cast<uint32_t*>(scratch + so) = fa | (fb << 16);
-      }
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(taddr, r[0]);
+      tmem_ld_32x32b_x32(taddr + 32, r[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      uint32_t cw[8], fs[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
+      __stcs(reinterpret_cast<uint4*>(crow), make_uint4(cw[0], cw[1], cw[2], cw[3]));
+      __stcs(reinterpret_cast<uint4*>(crow + 16), make_uint4(cw[4], cw[5], cw[6], cw[7]));
+      const int64_t kb = ogrp * 8 + colhalf * 4;  // 4 consecutive 16-blocks: one aligned 8-byte store
+      const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2);
+      *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) run_max = fmaxf(run_max, __shfl_xor_sync(0xffffffffu, run_max, o));
