@@ -208,13 +208,12 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       const float x_ts = *p.x_ts;
       const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
       constexpr int kItems = 128 * 8 / (32 * Cfg::kProdWarps);  // (row, 16-col group) items per thread
-      int it = 0;
-      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-        const int slot = it % kRhtStages;
-        const uint32_t ph = (it / kRhtStages) & 1;
+      // registers hold the next tile's codes and scales while this tile is
+      // converted, so global-load latency overlaps the conversion
+      uint2 q[kItems];
+      uint32_t sb[kItems];
+      auto load_tile = [&](int64_t t) {
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
-        uint2 q[kItems];
-        uint32_t sb[kItems];
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
@@ -226,16 +225,27 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
                              (kb & 3);
           sb[u] = p.x_sf[so];
         }
+      };
+      if (static_cast<int64_t>(blockIdx.x) < ntiles) load_tile(blockIdx.x);
+      int it = 0;
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int slot = it % kRhtStages;
+        const uint32_t ph = (it / kRhtStages) & 1;
+        uint2 qc[kItems];
+        uint32_t sc[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) { qc[u] = q[u]; sc[u] = sb[u]; }
+        if (t + gridDim.x < ntiles) load_tile(t + gridDim.x);
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
         uint8_t* dst = tiles + slot * kTileBytes;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
           const int r = item >> 3, g = item & 7;
-          const float gs = e4m3_to_f32(sb[u]) * x_ts;
+          const float gs = e4m3_to_f32(sc[u]) * x_ts;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {  // 8 elements -> one 16-byte chunk
-            const uint32_t w = half ? q[u].y : q[u].x;
+            const uint32_t w = half ? qc[u].y : qc[u].x;
             uint32_t o[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
