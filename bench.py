@@ -41,6 +41,11 @@ KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2
                     "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1}
 
 
+# Average DRAM bytes (read + write) per gemm_nvfp4_kernel launch over one step of this workload,
+# from the ncu launch list summarised in profiles/step_launches_4b_linear_set.txt.
+GEMM_DRAM_BYTES_PER_LAUNCH = 1843.1e6
+
+
 def flops_per_token() -> float:
     return 6.0 * sum(k * n for _, k, n in SHAPES)
 
@@ -213,7 +218,7 @@ def run_ours(args) -> None:
         comm = GradAllReduce([lay.weight for lay in layers])
 
     # bench-only instrumentation: kernel launches and GEMM launch durations
-    counters = {"launches": 0, "gemm_events": []}
+    counters = {"launches": 0, "gemm_events": [], "gemm_bytes": 0.0}
     orig_call = _lib.call
     state = {"timing": False}
 
@@ -233,7 +238,9 @@ def run_ours(args) -> None:
         s.record()
         out = orig_mm(x_fp4, w_fp4, x_mx, w_mx, alpha)
         e.record()
-        counters["gemm_events"].append((s, e, 2.0 * x_fp4.shape[0] * w_fp4.shape[0] * x_fp4.shape[1] * 2))
+        m, n, k = x_fp4.shape[0], w_fp4.shape[0], x_fp4.shape[1] * 2
+        counters["gemm_events"].append((s, e, 2.0 * m * n * k))
+        counters["gemm_bytes"] += m * k / 2 + n * k / 2 + (m + n) * k / 16 + 2 * m * n
         return out
 
     L._fp4_mm = timed_mm
@@ -273,6 +280,7 @@ def run_ours(args) -> None:
     gemm_ms = sum(s.elapsed_time(e) for s, e, _ in counters["gemm_events"])
     gemm_flops = sum(f for _, _, f in counters["gemm_events"])
     n_gemm = len(counters["gemm_events"])
+    gemm_alg_bytes = counters["gemm_bytes"]
     launches = counters["launches"] // args.steps
 
     # ---- end to end: inputs from pinned host memory, result read back, every step
@@ -336,7 +344,9 @@ def run_ours(args) -> None:
                         "memory each step, weight-gradient norms read back"},
         "roofline": {"bound": "tensor", "kernel": "gemm_nvfp4_kernel", "achieved": achieved,
                      "peak": fp4_peak, "unit": "TFLOP/s",
-                     "frac": (achieved / fp4_peak) if achieved else None, "traffic": None,
+                     "frac": (achieved / fp4_peak) if achieved else None,
+                     "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                     "algorithmic_bytes_per_launch": gemm_alg_bytes / max(n_gemm, 1),
                      "peak_note": "dense NVFP4 = 4 x measured sustained bf16 (MEASURED_PEAKS.json "
                                   f"{peaks['source']}); nominal dense fp4 9000 TFLOP/s",
                      "gemm_launches_per_step": n_gemm // max(args.steps, 1),
