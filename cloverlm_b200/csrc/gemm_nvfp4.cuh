@@ -38,6 +38,13 @@ struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BKB = 128;                 // bytes of K per stage (256 fp4)
   static constexpr int kStages = BN == 256 ? 4 : 6;
+  // Stages can be released and their scales published in groups of kGroup K
+  // blocks (one commit per group); measured slower for kGroup = 2, so 1.
+#ifndef Q2B_GEMM_GROUP
+#define Q2B_GEMM_GROUP 1
+#endif
+  static constexpr int kGroup = Q2B_GEMM_GROUP;
+  static_assert(kStages % kGroup == 0, "stages must form whole groups");
   static constexpr int kAccBufs = BN == 256 ? 1 : 2;
   static constexpr uint32_t kABytes = BM * BKB;   // 16 KB
   static constexpr uint32_t kBBytes = BN * BKB;
@@ -51,7 +58,13 @@ struct GemmCfg {
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
   static constexpr int kEpiWarps = 8;
-  static constexpr int kEpiWarp0 = 3;
+#ifndef Q2B_GEMM_SF_WARPS
+#define Q2B_GEMM_SF_WARPS 2
+#endif
+  // scale copies are issued by kSfWarps warps (A scales / B scales) because
+  // tcgen05 issue blocks per thread: two issuing threads copy concurrently
+  static constexpr int kSfWarps = Q2B_GEMM_SF_WARPS;
+  static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
 };
@@ -92,7 +105,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&sfready[s], 1);
+      mbar_init(&sfready[s], Cfg::kSfWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -122,7 +135,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
         for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
           const int slot = static_cast<int>(it % Cfg::kStages);
           const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+          if (slot % Cfg::kGroup == 0 &&
+              !mbar_wait(&empty[slot / Cfg::kGroup], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
 #ifdef Q2B_GEMM_PROBE_NO_TMA
           if (true) { mbar_arrive(&full[slot]); continue; }
 #endif
@@ -144,72 +158,86 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
         mbar_wait(&full[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
     }
-  } else if (warp == 2) {
+  } else if (warp >= 2 && warp < 2 + Cfg::kSfWarps) {
     // ------------------------------------------------------------ scale copies
-    // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
-    const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
-    const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
-    int64_t it = 0;
-    bool ok = true;
-    for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
-        const int slot = static_cast<int>(it % Cfg::kStages);
-        const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-        if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
-        tc_fence_after();
-        if (lane == 0) {
+    const int role = Cfg::kSfWarps == 1 ? 2 : warp - 2;  // 0: A scales, 1: B scales, 2: both
+    if (lane == 0) {
+      // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
+      const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
+      const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
+      int slot = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        for (int64_t kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
           const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-          const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+          const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
           const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+#ifndef Q2B_GEMM_PROBE_NO_SFCP
           for (int j = 0; j < nk; ++j) {
-            tmem_cp_32x128b_x4(set + 4 * j, sfa_d0 + so + 32 * j);
+            if (role != 1) tmem_cp_32x128b_x4(set + 4 * j, sfa_d0 + so + 32 * j);
+            if (role != 0) {
 #pragma unroll
-            for (int u = 0; u < BN / 128; ++u)
-              tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
+              for (int u = 0; u < BN / 128; ++u)
+                tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
+            }
           }
-          tc_commit(&sfready[slot]);
+#else
+          (void)nk; (void)so; (void)set;
+#endif
+          if (slot % Cfg::kGroup == Cfg::kGroup - 1 || (kb == nkb - 1 && t + gridDim.x >= ntiles))
+            tc_commit(&sfready[slot / Cfg::kGroup]);
+          if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
-        __syncwarp();
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    const uint32_t idesc = idesc_nvf4(Cfg::BM, BN);
-    const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
-    const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
-    int64_t it = 0, tc = 0;
-    bool ok = true;
-    for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
-      const int buf = static_cast<int>(tc % Cfg::kAccBufs);
-      const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
-      if (!mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty)) break;
-      tc_fence_after();
-      const uint32_t d = tmem + buf * BN;
-      for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
-        const int slot = static_cast<int>(it % Cfg::kStages);
-        const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-        if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+    // tcgen05.mma issue blocks until the pipe can take it, so the issuing
+    // thread keeps its loop minimal: lane 0 alone, incremental slot/phase,
+    // precomputed descriptors, no warp-wide sync per K block.
+    if (lane == 0) {
+      const uint32_t idesc = idesc_nvf4(Cfg::BM, BN);
+      const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
+      const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
+      const uint32_t sf0 = tmem + Cfg::kSfBase;
+      int slot = 0;
+      uint32_t ph = 0;
+      int64_t tc = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+        const int buf = static_cast<int>(tc % Cfg::kAccBufs);
+        const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
+        if (!mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty)) break;
         tc_fence_after();
-        if (lane == 0) {
-          const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
-          const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+        const uint32_t d = tmem + buf * BN;
+        for (int64_t kb = 0; kb < nkb; ++kb) {
+          if (slot % Cfg::kGroup == 0) {
+            if (!mbar_wait(&sfready[slot / Cfg::kGroup], ph, kTimeoutTmaFull)) { ok = false; break; }
+            tc_fence_after();
+          }
+          const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
+          const uint32_t set = sf0 + slot * Cfg::kSfSetCols;
+          const uint64_t ad = a_d0 + so, bd = b_d0 + so;
           if (kb == nkb - 1 && tail_nk) {
             for (int j = 0; j < tail_nk; ++j)
-              umma_nvf4(d, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
+              umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
                         (kb > 0 || j > 0) ? 1u : 0u);
           } else {
+            umma_nvf4(d, ad, bd, idesc, set, set + 16, kb > 0 ? 1u : 0u);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              umma_nvf4(d, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
-                        (kb > 0 || j > 0) ? 1u : 0u);
+            for (int j = 1; j < 4; ++j)
+              umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j, 1u);
           }
-          tc_commit(&empty[slot]);
+          if (slot % Cfg::kGroup == Cfg::kGroup - 1 || (kb == nkb - 1 && t + gridDim.x >= ntiles))
+            tc_commit(&empty[slot / Cfg::kGroup]);
+          if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
-        __syncwarp();
+        if (!ok) break;
+        tc_commit(&tfull[buf]);
       }
-      if (!ok) break;
-      if (lane == 0) tc_commit(&tfull[buf]);
-      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue
