@@ -276,6 +276,18 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
   return r;
 }
 
+// Two fp32 -> packed E2M1 byte (as in cvt_e2m1x2) and, from the same byte
+// register, its two decoded values as fp16x2 -- one asm block, so the byte
+// never round-trips through a 32-bit register between the conversions.
+__device__ __forceinline__ void cvt_e2m1x2_back(float lo, float hi, uint32_t& byte, uint32_t& back_h2) {
+  asm("{\n\t.reg .b8 b;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b, %2, %3;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b;\n\t"
+      "cvt.u32.u8 %0, b;\n\t}"
+      : "=r"(byte), "=r"(back_h2)
+      : "f"(hi), "f"(lo));
+}
+
 // Packed E2M1 byte -> two fp16 values (low nibble in the low half).
 __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   uint32_t r;

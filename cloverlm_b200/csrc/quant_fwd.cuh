@@ -56,21 +56,21 @@ __device__ __forceinline__ float quant16(const float (&xs)[16], const float (&xa
   s8 = cvt_e4m3(gabs * inv_c * inv_ts);
   const float f = tab.factor[s8];
   const float nd = -tab.descale[s8];
-  uint32_t b[8];
+  uint32_t b[8], h[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const float2 w = fmul2(make_float2(xs[2 * k], xs[2 * k + 1]), make_float2(f, f));
-    b[k] = cvt_e2m1x2(w.x, w.y);
+    cvt_e2m1x2_back(w.x, w.y, b[k], h[k]);
   }
   codes.x = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
   codes.y = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
   float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float2 q0 = f16x2_to_f32x2(e2m1x2_to_f16x2(b[k] & 0x77u));
+    const float2 q0 = f16x2_to_f32x2(h[k] & 0x7FFF7FFFu);
     const float2 d0 = ffma2(q0, make_float2(nd, nd), make_float2(xa[2 * k], xa[2 * k + 1]));
     s0 = ffma2(d0, d0, s0);
-    const float2 q1 = f16x2_to_f32x2(e2m1x2_to_f16x2(b[4 + k] & 0x77u));
+    const float2 q1 = f16x2_to_f32x2(h[4 + k] & 0x7FFF7FFFu);
     const float2 d1 = ffma2(q1, make_float2(nd, nd), make_float2(xa[8 + 2 * k], xa[8 + 2 * k + 1]));
     s1 = ffma2(d1, d1, s1);
   }
@@ -102,8 +102,7 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
   for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
     uint32_t w[8];
     ldg256(x + static_cast<uint64_t>(g) * 16, w);
-    float xs[16], xa[16];
-    float gabs = 0.f;
+    float xs[16], xa[16], m[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       xs[2 * k] = bf16lo(w[k]);
@@ -111,8 +110,11 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
       const uint32_t a = w[k] & 0x7FFF7FFFu;
       xa[2 * k] = bf16lo(a);
       xa[2 * k + 1] = bf16hi(a);
-      gabs = fmaxf(gabs, fmaxf(xa[2 * k], xa[2 * k + 1]));
+      m[k] = fmaxf(xa[2 * k], xa[2 * k + 1]);
     }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m[k] = fmaxf(m[k], m[k + 4]);
+    const float gabs = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
     uint2 c;
     uint32_t s;
     const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, s);

@@ -109,24 +109,31 @@ __device__ __forceinline__ void build_rotation(uint8_t* hs, const uint16_t* h, i
 // the bf16-rounded fixed scale as fp32.
 __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, uint32_t& w0, uint32_t& w1,
                                         uint32_t& fixed_bf16) {
-  float amax = 0.f;
+  // abs-max as a depth-4 tree (max is order-independent)
+  float m[8];
 #pragma unroll
-  for (int t = 0; t < 16; ++t) amax = fmaxf(amax, fabsf(__uint_as_float(r[t])));
+  for (int t = 0; t < 8; ++t) m[t] = fmaxf(fabsf(__uint_as_float(r[2 * t])), fabsf(__uint_as_float(r[2 * t + 1])));
+#pragma unroll
+  for (int t = 0; t < 4; ++t) m[t] = fmaxf(m[t], m[t + 4]);
+  const float amax = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
   const float scale = amax * inv_fp4_max;
   float m3 = __uint_as_float(__float_as_uint(scale) & 0xFFF80000u);
   float f;
   if (fabsf(m3) < FLT_MIN) { m3 = 0.f; f = 0.f; } else { f = rcp_rn(m3); }
   float2 xx = make_float2(0.f, 0.f), xy = make_float2(0.f, 0.f);
-  uint32_t c[2] = {0u, 0u};
+  uint32_t b[8];
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     const float2 w = fmul2(make_float2(__uint_as_float(r[2 * t]), __uint_as_float(r[2 * t + 1])), make_float2(f, f));
-    const uint32_t b = cvt_e2m1x2(w.x, w.y);
-    const float2 back = f16x2_to_f32x2(e2m1x2_to_f16x2(b));
+    uint32_t h2;
+    cvt_e2m1x2_back(w.x, w.y, b[t], h2);
+    const float2 back = f16x2_to_f32x2(h2);
     xx = ffma2(w, w, xx);
     xy = ffma2(w, back, xy);
-    c[t >> 2] |= b << (8 * (t & 3));
   }
+  uint32_t c[2];
+  c[0] = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
+  c[1] = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
   const float xx_t = xx.x + xx.y, xy_t = xy.x + xy.y;
   const float corr = (xy_t == 0.f) ? 1.f : xx_t * rcp_rn(xy_t);
   const float fixed = m3 * corr;
