@@ -59,7 +59,7 @@ struct GemmCfg {
   static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
   static constexpr int kEpiWarps = 8;
 #ifndef Q2B_GEMM_SF_WARPS
-#define Q2B_GEMM_SF_WARPS 2
+#define Q2B_GEMM_SF_WARPS 6
 #endif
   // scale copies are issued by kSfWarps warps (A scales / B scales) because
   // tcgen05 issue blocks per thread: two issuing threads copy concurrently
@@ -160,7 +160,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     }
   } else if (warp >= 2 && warp < 2 + Cfg::kSfWarps) {
     // ------------------------------------------------------------ scale copies
-    const int role = Cfg::kSfWarps == 1 ? 2 : warp - 2;  // 0: A scales, 1: B scales, 2: both
+    const int me = warp - 2;
+    constexpr int kPerStep = 1 + BN / 128;
     if (lane == 0) {
       // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
       const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
@@ -176,12 +177,16 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
           const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
 #ifndef Q2B_GEMM_PROBE_NO_SFCP
-          for (int j = 0; j < nk; ++j) {
-            if (role != 1) tmem_cp_32x128b_x4(set + 4 * j, sfa_d0 + so + 32 * j);
-            if (role != 0) {
-#pragma unroll
-              for (int u = 0; u < BN / 128; ++u)
-                tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
+          // copies in TMEM column order (A steps, then B steps x halves);
+          // each warp takes a contiguous block of them
+          const int ncp = nk * kPerStep;
+          const int lo = me * ncp / Cfg::kSfWarps, hi = (me + 1) * ncp / Cfg::kSfWarps;
+          for (int c = lo; c < hi; ++c) {
+            if (c < nk) {
+              tmem_cp_32x128b_x4(set + 4 * c, sfa_d0 + so + 32 * c);
+            } else {
+              const int b = c - nk, j = b / (BN / 128), u = b % (BN / 128);
+              tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
             }
           }
 #else
@@ -256,26 +261,33 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       const int64_t row = tm * Cfg::BM + q * 32 + lane;
       __nv_bfloat16* drow = p.D + row * p.N + tn * BN + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + c0;
-      // Drain the whole accumulator slice into registers first and hand the
-      // TMEM buffer back to the MMA warp at once; the bf16 conversion and the
-      // global stores then overlap the next tile's MMAs.
+      // Drain the whole accumulator slice into registers first (scaled and
+      // packed to bf16 pairs in two halves, which halves the live registers)
+      // and hand the TMEM buffer back to the MMA warp at once; the global
+      // stores then overlap the next tile's MMAs.
       constexpr int kChunks = kColsPerWarp / 32;
-      uint32_t r[kChunks][32];
+      constexpr int kHalf = kChunks > 1 ? kChunks / 2 : 1;
+      uint32_t o[kChunks][16];
 #pragma unroll
-      for (int ch = 0; ch < kChunks; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
-      tmem_ld_wait();
+      for (int h0 = 0; h0 < kChunks; h0 += kHalf) {
+        uint32_t r[kHalf][32];
+#pragma unroll
+        for (int ch = 0; ch < kHalf; ++ch) tmem_ld_32x32b_x32(taddr + (h0 + ch) * 32, r[ch]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int ch = 0; ch < kHalf; ++ch)
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o[h0 + ch][k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
 #pragma unroll
       for (int ch = 0; ch < kChunks; ++ch) {
-        uint32_t o[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
         uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
       }
     }
   }
@@ -300,11 +312,17 @@ namespace q2b {
 // fit.  Scale factors: each CTA holds the A scales of its rows and the B
 // scales of all 256 columns (four-way lane-replicated, as tcgen05.cp 32x128b
 // .warpx4 writes them); one 2-CTA copy instruction fills both CTAs' TMEM.
-//   leader (rank 0): TMA warp, MMA warp, epilogue; its full[] barriers count
-//                    the bytes of BOTH CTAs (.cta_group::2 TMA completes on
-//                    the leader's barrier), its tempty[] collects both CTAs'
-//                    epilogue warps.
+//   leader (rank 0): TMA warp, MMA warp, one scale-copy warp per ring slot,
+//                    epilogue; its full[] barriers count the bytes of BOTH
+//                    CTAs (.cta_group::2 TMA completes on the leader's
+//                    barrier), its tempty[] collects both CTAs' epilogue warps.
 //   peer   (rank 1): TMA warp and epilogue.
+// tcgen05 issue blocks the issuing thread while the tensor pipe is busy, and
+// copies issued from separate warps proceed concurrently with each other and
+// with the MMAs; one thread issuing all twelve copies of a K block would
+// stall the MMA stream (measured: 2 copy warps 1.0k cycles per K block, 5-6
+// warps 0.6-0.7k, MMAs alone 0.51k).  Hence a copy warp per ring slot, each
+// committing once per K block.
 // Every wait is bounded; both CTAs meet at a cluster barrier before TMEM is
 // freed and before exit, so no CTA leaves while its peer can still touch its
 // shared memory or TMEM.
@@ -318,7 +336,8 @@ struct Gemm2Cfg {
   static constexpr uint32_t kSfSetCols = 48, kSfBase = 256, kTmemCols = 512;
   static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
   static constexpr int kEpiWarps = 8;
-  static constexpr int kEpiWarp0 = 3;
+  static constexpr int kSfWarps = kStages;  // copy warp w owns ring slot w
+  static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
 };
@@ -336,8 +355,9 @@ __device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
 // Warp roles (both CTAs unless noted):
 //   0  TMA producer; its loads complete on the LEADER's full[s]
 //   1  MMA issuer (leader): waits sfready[s], cta_group::2 MMAs, multicast-commits empty[s]
-//   2  scale-copy issuer (leader): waits full[s], cta_group::2 tcgen05.cp into set s, commits sfready[s]
-//   3+ epilogue: drains its own TMEM rows, arrives on the leader's tempty
+//   2..kEpiWarp0-1  scale-copy issuers (leader): warp 2+s waits full[s], issues the stage's
+//      cta_group::2 tcgen05.cp into TMEM set s, commits sfready[s]
+//   kEpiWarp0+  epilogue: drains its own TMEM rows, arrives on the leader's tempty
 __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
@@ -353,6 +373,17 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef Q2B_GEMM_PROBE_TIMING
+  __shared__ long long t_issue[Gemm2Cfg::kStages], t_mma[Gemm2Cfg::kStages];
+  volatile long long* vt_issue = t_issue;
+  volatile long long* vt_mma = t_mma;
+  long long acc_wait = 0, acc_lat = 0, nacc = 0;
+#define Q2B_T0 const long long _t0 = clock64();
+#define Q2B_TW acc_wait += clock64() - _t0; ++nacc;
+#else
+#define Q2B_T0
+#define Q2B_TW
+#endif
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -403,7 +434,16 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
           const int slot = static_cast<int>(it % Cfg::kStages);
           const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+          Q2B_T0
           if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+          Q2B_TW
+#ifdef Q2B_GEMM_PROBE_TIMING
+          if (it >= Cfg::kStages) acc_lat += clock64() - vt_mma[slot];
+          vt_issue[slot] = clock64();
+#endif
+#ifdef Q2B_GEMM_PROBE_NO_TMA
+          if (true) { if (leader) mbar_arrive(&full[slot]); continue; }
+#endif
           uint8_t* st = smem + slot * Cfg::kStageBytes;
           const uint32_t bar = map_to_rank(smem_u32(&full[slot]), 0);
           if (leader) mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kStageBytes);
@@ -423,65 +463,69 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
         mbar_wait(&empty[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
     }
-  } else if (warp == 2) {
+  } else if (warp >= 2 && warp < Cfg::kEpiWarp0) {
     // ------------------------------------------------------------ scale copies (leader)
-    if (leader) {
+    if (leader && lane == 0) {
+      const int me = warp - 2;
       const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
       const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
-      int64_t it = 0;
-      bool ok = true;
-      for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
-          const int slot = static_cast<int>(it % Cfg::kStages);
-          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-          if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
-          tc_fence_after();
-          if (lane == 0) {
-            const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-            const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
-            const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
-            for (int j = 0; j < nk; ++j) {
-              tmem_cp_32x128b_x4_pair(set + 4 * j, sfa_d0 + so + 32 * j);
-              tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + so + 32 * j);
-              tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + so + 128 + 32 * j);
-            }
-            tc_commit_pair_leader(&sfready[slot]);
-          }
-          __syncwarp();
+      // copy warp `me` serves every K block that lands in ring slot `me`
+      const int64_t my_tiles = cluster_id < ntiles ? (ntiles - 1 - cluster_id) / nclusters + 1 : 0;
+      const int64_t total = my_tiles * nkb;
+      const int slot = me;
+      const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+      const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+      for (int64_t i = me; i < total; i += Cfg::kStages) {
+        const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1;
+        const int64_t kb = i % nkb;
+        Q2B_T0
+        if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) break;
+        Q2B_TW
+        tc_fence_after();
+        const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+        for (int j = 0; j < nk; ++j) {
+          tmem_cp_32x128b_x4_pair(set + 4 * j, sfa_d0 + so + 32 * j);
+          tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + so + 32 * j);
+          tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + so + 128 + 32 * j);
         }
+        tc_commit_pair_leader(&sfready[slot]);
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issue (leader)
-    if (leader) {
+    // ------------------------------------------------------------ MMA issue (leader, lane 0)
+    if (leader && lane == 0) {
       const uint32_t idesc = idesc_nvf4(256, 256);
       const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
       const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
-      int64_t it = 0, tc = 0;
+      int slot = 0;
+      uint32_t ph = 0;
+      int64_t tc = 0;
       bool ok = true;
       for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters, ++tc) {
         const uint32_t bph = static_cast<uint32_t>(tc) & 1;
         if (!mbar_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
         tc_fence_after();
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
-          const int slot = static_cast<int>(it % Cfg::kStages);
-          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+        for (int64_t kb = 0; kb < nkb; ++kb) {
+#ifndef Q2B_GEMM_PROBE_NO_SFWAIT
+          Q2B_T0
           if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          Q2B_TW
+#endif
+#ifdef Q2B_GEMM_PROBE_TIMING
+          vt_mma[slot] = clock64();
+#endif
           tc_fence_after();
-          if (lane == 0) {
-            const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
-            const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
-            const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-            for (int j = 0; j < nk; ++j)
-              umma_nvf4_pair(tmem, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
-                             (kb > 0 || j > 0) ? 1u : 0u);
-            tc_commit_pair(&empty[slot]);
-          }
-          __syncwarp();
+          const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
+          const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+          const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+          for (int j = 0; j < nk; ++j)
+            umma_nvf4_pair(tmem, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
+                           (kb > 0 || j > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[slot]);
+          if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
         if (!ok) break;
-        if (lane == 0) tc_commit_pair(tfull);
-        __syncwarp();
+        tc_commit_pair(tfull);
       }
     }
   } else {
@@ -499,26 +543,39 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       const int64_t row = tm * 256 + rank * 128 + q * 32 + lane;
       __nv_bfloat16* drow = p.D + row * p.N + tn * 256 + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
-      uint32_t r[4][32];
+      uint32_t o[4][16];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
-      tmem_ld_wait();
+      for (int h0 = 0; h0 < 4; h0 += 2) {
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(taddr + h0 * 32, r[0]);
+        tmem_ld_32x32b_x32(taddr + h0 * 32 + 32, r[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o[h0 + ch][k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
+#ifdef Q2B_GEMM_PROBE_NO_STORE
+      if (o[0][0] != 0x12345678u) continue;
+#endif
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        uint32_t o[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
         uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
       }
     }
   }
 
+#ifdef Q2B_GEMM_PROBE_TIMING
+  if (blockIdx.x == 0 && lane == 0 && warp < 3 && nacc > 0)
+    printf("probe warp %d: %lld K blocks, wait %.0f cycles/kb, latency %.0f cycles/kb\n", warp, nacc,
+           (double)acc_wait / nacc, (double)acc_lat / nacc);
+#endif
   tc_fence_before();
   cluster_sync();
   if (warp == 1) {

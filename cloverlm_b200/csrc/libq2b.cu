@@ -448,7 +448,7 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
   q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha,
                     static_cast<__nv_bfloat16*>(D)};
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, 128, 128)) return r;
-#ifdef Q2B_GEMM_USE_2SM
+#ifndef Q2B_GEMM_NO_2SM
   if (M % 256 == 0 && N % 256 == 0 && sms >= 2) {
     // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair
     CUtensorMap tsa, tsb;
