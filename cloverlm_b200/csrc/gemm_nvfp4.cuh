@@ -335,7 +335,10 @@ struct Gemm2Cfg {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 38 KB
   static constexpr uint32_t kSfSetCols = 48, kSfBase = 256, kTmemCols = 512;
   static_assert(kSfBase + kStages * kSfSetCols <= kTmemCols, "TMEM overflow");
-  static constexpr int kEpiWarps = 8;
+#ifndef Q2B_GEMM2_EPI_WARPS
+#define Q2B_GEMM2_EPI_WARPS 16
+#endif
+  static constexpr int kEpiWarps = Q2B_GEMM2_EPI_WARPS;  // 4 per TMEM lane quarter, 64 columns each
   static constexpr int kSfWarps = kStages;  // copy warp w owns ring slot w
   static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
@@ -503,7 +506,13 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       bool ok = true;
       for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters, ++tc) {
         const uint32_t bph = static_cast<uint32_t>(tc) & 1;
+#ifdef Q2B_GEMM_PROBE_TIMING
+        const long long _te = clock64();
+#endif
         if (!mbar_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
+#ifdef Q2B_GEMM_PROBE_TIMING
+        acc_lat += clock64() - _te;
+#endif
         tc_fence_after();
         for (int64_t kb = 0; kb < nkb; ++kb) {
 #ifndef Q2B_GEMM_PROBE_NO_SFWAIT
@@ -532,50 +541,56 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int e = warp - Cfg::kEpiWarp0;
     const int q = warp & 3;
-    const int c0 = (e >> 2) * 128;
+    constexpr int kCols = 256 / (Cfg::kEpiWarps / 4);  // columns per warp
+    const int c0 = (e >> 2) * kCols;
     const float alpha = *p.alpha;
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
+#ifdef Q2B_GEMM_PROBE_TIMING
+      const long long _tf = clock64();
+#endif
       if (!mbar_wait(tfull, static_cast<uint32_t>(tc) & 1, kTimeoutTmemFull)) break;
+#ifdef Q2B_GEMM_PROBE_TIMING
+      const long long _tg = clock64();
+      acc_wait += _tg - _tf;
+      ++nacc;
+#endif
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
       const int64_t row = tm * 256 + rank * 128 + q * 32 + lane;
       __nv_bfloat16* drow = p.D + row * p.N + tn * 256 + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
-      uint32_t o[4][16];
+      // One TMEM round trip for the warp's whole slice, then the accumulator
+      // goes back to the MMA warp; scaling, packing and stores follow.
+      uint32_t r[kCols / 32][32];
 #pragma unroll
-      for (int h0 = 0; h0 < 4; h0 += 2) {
-        uint32_t r[2][32];
-        tmem_ld_32x32b_x32(taddr + h0 * 32, r[0]);
-        tmem_ld_32x32b_x32(taddr + h0 * 32 + 32, r[1]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            o[h0 + ch][k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
-      }
+      for (int ch = 0; ch < kCols / 32; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-#ifdef Q2B_GEMM_PROBE_NO_STORE
-      if (o[0][0] != 0x12345678u) continue;
+#ifdef Q2B_GEMM_PROBE_TIMING
+      acc_lat += clock64() - _tg;
 #endif
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+      for (int ch = 0; ch < kCols / 32; ++ch) {
+        uint32_t o[16];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
+        for (int k = 0; k < 16; ++k)
+          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
+#ifdef Q2B_GEMM_PROBE_NO_STORE
+        if (o[0] == 0x12345678u)
+#endif
+        {
+          uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        }
       }
     }
   }
 
-#ifdef Q2B_GEMM_PROBE_TIMING
-  if (blockIdx.x == 0 && lane == 0 && warp < 3 && nacc > 0)
-    printf("probe warp %d: %lld K blocks, wait %.0f cycles/kb, latency %.0f cycles/kb\n", warp, nacc,
-           (double)acc_wait / nacc, (double)acc_lat / nacc);
-#endif
   tc_fence_before();
   cluster_sync();
   if (warp == 1) {
