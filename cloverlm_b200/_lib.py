@@ -38,6 +38,8 @@ SIGNATURES = {
     "q2b_rht_eden_dual": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _P, _U64, _U64, _F, _F, _I64, _I64, _P],
     "q2b_rht_requant": [_P, _P, _P, _P, _P, _P, _INT, _P, _P, _P, _U64, _F, _F, _I64, _I64, _P],
     "q2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "q2b_quant_fwd_ragged": [_P, _P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
+    "q2b_gemm_nvfp4_ex": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P],
 }
 
 _lib = None
@@ -64,6 +66,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn.restype = _INT
         lib.q2b_last_error.argtypes = []
         lib.q2b_last_error.restype = ctypes.c_char_p
+        lib.q2b_gemm_workspace_bytes.argtypes = [_I64, _I64, _I64]
+        lib.q2b_gemm_workspace_bytes.restype = _I64
         lib.q2b_version.argtypes = []
         lib.q2b_version.restype = _INT
         _lib = lib

@@ -26,11 +26,15 @@
 namespace q2b {
 
 struct GemmParams {
-  int64_t M, N, K;
+  int64_t M, N, K;      // M rounded up to whole 128-row tiles
   const uint8_t* sfa;   // blocked [M, K/16]
   const uint8_t* sfb;   // blocked [N, K/16]
   const float* alpha;
-  __nv_bfloat16* D;     // [M, N] row-major
+  __nv_bfloat16* D;     // [m_valid, N] row-major
+  int64_t m_valid;      // rows of A and D that exist (A rows past it read as zero through TMA)
+  int splits;           // K split into this many ranges per output tile (1 = none)
+  float* ws;            // splits > 1: fp32 partial tiles [tiles][128][BN], zero between calls
+  unsigned* counters;   // splits > 1: arrival counters [tiles][epilogue warps], zero between calls
 };
 
 template <int BN>
@@ -38,13 +42,6 @@ struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BKB = 128;                 // bytes of K per stage (256 fp4)
   static constexpr int kStages = BN == 256 ? 4 : 6;
-  // Stages can be released and their scales published in groups of kGroup K
-  // blocks (one commit per group); measured slower for kGroup = 2, so 1.
-#ifndef Q2B_GEMM_GROUP
-#define Q2B_GEMM_GROUP 1
-#endif
-  static constexpr int kGroup = Q2B_GEMM_GROUP;
-  static_assert(kStages % kGroup == 0, "stages must form whole groups");
   static constexpr int kAccBufs = BN == 256 ? 1 : 2;
   static constexpr uint32_t kABytes = BM * BKB;   // 16 KB
   static constexpr uint32_t kBBytes = BN * BKB;
@@ -97,6 +94,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles_n = p.N / BN;
   const int64_t ntiles = (p.M / Cfg::BM) * tiles_n;
+  const int splits = p.splits;
+  const int64_t nunits = ntiles * splits;  // work unit = (output tile, K range)
   const int64_t nkb = (p.K + 255) / 256;
   const int64_t n_kt = p.K / 64;  // 64-element scale chunks along K
   const int tail_nk = static_cast<int>((p.K % 256) / 64);  // K steps in a partial last block (0 = none)
@@ -130,13 +129,13 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     if (lane == 0) {
       int64_t it = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const int64_t t = u / splits, sp = u % splits;
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+        for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb, ++it) {
           const int slot = static_cast<int>(it % Cfg::kStages);
           const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-          if (slot % Cfg::kGroup == 0 &&
-              !mbar_wait(&empty[slot / Cfg::kGroup], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
 #ifdef Q2B_GEMM_PROBE_NO_TMA
           if (true) { mbar_arrive(&full[slot]); continue; }
 #endif
@@ -169,8 +168,9 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       int slot = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        for (int64_t kb = 0; kb < nkb; ++kb) {
+      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const int64_t sp = u % splits;
+        for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb) {
           if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
           tc_fence_after();
           const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
@@ -192,8 +192,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
 #else
           (void)nk; (void)so; (void)set;
 #endif
-          if (slot % Cfg::kGroup == Cfg::kGroup - 1 || (kb == nkb - 1 && t + gridDim.x >= ntiles))
-            tc_commit(&sfready[slot / Cfg::kGroup]);
+          tc_commit(&sfready[slot]);
           if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
       }
@@ -212,32 +211,30 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       uint32_t ph = 0;
       int64_t tc = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++tc) {
         const int buf = static_cast<int>(tc % Cfg::kAccBufs);
         const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
         if (!mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int64_t kb = 0; kb < nkb; ++kb) {
-          if (slot % Cfg::kGroup == 0) {
-            if (!mbar_wait(&sfready[slot / Cfg::kGroup], ph, kTimeoutTmaFull)) { ok = false; break; }
-            tc_fence_after();
-          }
+        const int64_t sp = u % splits, kb0 = sp * nkb / splits;
+        for (int64_t kb = kb0; kb < (sp + 1) * nkb / splits; ++kb) {
+          if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
           const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
           const uint32_t set = sf0 + slot * Cfg::kSfSetCols;
           const uint64_t ad = a_d0 + so, bd = b_d0 + so;
           if (kb == nkb - 1 && tail_nk) {
             for (int j = 0; j < tail_nk; ++j)
               umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
-                        (kb > 0 || j > 0) ? 1u : 0u);
+                        (kb > kb0 || j > 0) ? 1u : 0u);
           } else {
-            umma_nvf4(d, ad, bd, idesc, set, set + 16, kb > 0 ? 1u : 0u);
+            umma_nvf4(d, ad, bd, idesc, set, set + 16, kb > kb0 ? 1u : 0u);
 #pragma unroll
             for (int j = 1; j < 4; ++j)
               umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j, 1u);
           }
-          if (slot % Cfg::kGroup == Cfg::kGroup - 1 || (kb == nkb - 1 && t + gridDim.x >= ntiles))
-            tc_commit(&empty[slot / Cfg::kGroup]);
+          tc_commit(&empty[slot]);
           if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -252,20 +249,76 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     const int c0 = (e >> 2) * kColsPerWarp;
     const float alpha = *p.alpha;
     int64_t tc = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+    for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x, ++tc) {
       const int buf = static_cast<int>(tc % Cfg::kAccBufs);
       const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
       tc_fence_after();
+      const int64_t t = u / splits;
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
-      const int64_t row = tm * Cfg::BM + q * 32 + lane;
+      const int trow = q * 32 + lane;
+      const int64_t row = tm * Cfg::BM + trow;
+      const bool live = row < p.m_valid;
       __nv_bfloat16* drow = p.D + row * p.N + tn * BN + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + c0;
+      constexpr int kChunks = kColsPerWarp / 32;
+      if constexpr (BN == 128) {
+        if (splits > 1) {
+          // Split-K: add this K range's partial (times alpha) into the fp32
+          // tile in the workspace; the unit that arrives last converts the
+          // tile to bf16, stores it and zeroes the workspace and counter.
+          uint32_t r[kChunks][32];
+#pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+          float* wrow = p.ws + t * (Cfg::BM * BN) + trow * BN + c0;
+          if (live) {
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch)
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                red_add_v4(wrow + ch * 32 + 4 * k, __uint_as_float(r[ch][4 * k]) * alpha,
+                           __uint_as_float(r[ch][4 * k + 1]) * alpha, __uint_as_float(r[ch][4 * k + 2]) * alpha,
+                           __uint_as_float(r[ch][4 * k + 3]) * alpha);
+          }
+          // each epilogue warp owns a 32-row x 64-column region of the tile
+          // and its own arrival counter, so no barrier spans warps
+          __threadfence();
+          __syncwarp();
+          unsigned* ctr = p.counters + t * Cfg::kEpiWarps + e;
+          int last = 0;
+          if (lane == 0) last = atomicAdd(ctr, 1u) == static_cast<unsigned>(splits - 1);
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
+            __threadfence();
+            if (live) {
+#pragma unroll
+              for (int ch = 0; ch < kChunks; ++ch) {
+                uint32_t o[16];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const float4 v = __ldcg(reinterpret_cast<const float4*>(wrow + ch * 32 + 4 * k));
+                  o[2 * k] = pack_bf16x2(v.x, v.y);
+                  o[2 * k + 1] = pack_bf16x2(v.z, v.w);
+                  __stcg(reinterpret_cast<float4*>(wrow + ch * 32 + 4 * k), make_float4(0.f, 0.f, 0.f, 0.f));
+                }
+                uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+              }
+            }
+            if (lane == 0) *ctr = 0u;
+          }
+          continue;
+        }
+      }
       // Drain the whole accumulator slice into registers first (scaled and
       // packed to bf16 pairs in two halves, which halves the live registers)
       // and hand the TMEM buffer back to the MMA warp at once; the global
       // stores then overlap the next tile's MMAs.
-      constexpr int kChunks = kColsPerWarp / 32;
       constexpr int kHalf = kChunks > 1 ? kChunks / 2 : 1;
       uint32_t o[kChunks][16];
 #pragma unroll
@@ -283,11 +336,13 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (live) {
 #pragma unroll
-      for (int ch = 0; ch < kChunks; ++ch) {
-        uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+        for (int ch = 0; ch < kChunks; ++ch) {
+          uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
+          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
+        }
       }
     }
   }

@@ -201,13 +201,17 @@ int q2b_abs_max(float* out, const void* x, int64_t n, void* stream) {
   return Q2B_OK;
 }
 
-int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
-                  int64_t rows, int64_t cols, int mode, void* stream) {
+static int quant_fwd_impl(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                          int64_t rows, int64_t cols, int mode, void* stream, bool ragged) {
   if (mode != Q2B_MODE_RNE && mode != Q2B_MODE_FOUR_SIX)
     return fail(Q2B_ERR_INVALID, "quant_fwd: unknown mode %d", mode);
   const char* name = mode == Q2B_MODE_RNE ? "rtn_fp4" : "four_six_fp4";
   if (cols % 128 != 0) return fail(Q2B_ERR_INVALID, "%s: cols must be divisible by 128", name);
-  if (int r = check_dims128(name, rows, cols)) return r;
+  if (ragged) {
+    if (rows <= 0) return fail(Q2B_ERR_INVALID, "%s: rows must be positive", name);
+  } else if (int r = check_dims128(name, rows, cols)) {
+    return r;
+  }
   Q2B_REQUIRE_PTR(codes);
   Q2B_REQUIRE_PTR(sf);
   Q2B_REQUIRE_PTR(x);
@@ -235,6 +239,16 @@ int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* 
         scale_override, static_cast<uint32_t>(ngroups), gpr, magic);
   Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
+}
+
+int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                  int64_t rows, int64_t cols, int mode, void* stream) {
+  return quant_fwd_impl(codes, sf, ts, x, amax, scale_override, rows, cols, mode, stream, false);
+}
+
+int q2b_quant_fwd_ragged(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                         int64_t rows, int64_t cols, int mode, void* stream) {
+  return quant_fwd_impl(codes, sf, ts, x, amax, scale_override, rows, cols, mode, stream, true);
 }
 
 int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h, int h_rows,
@@ -429,27 +443,48 @@ int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* s
   return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
 }
 
-int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
-                   int64_t M, int64_t N, int64_t K, void* stream) {
-  if (M <= 0 || N <= 0 || K <= 0) return fail(Q2B_ERR_INVALID, "fp4_mm: empty problem");
-  if (M % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: M must be divisible by 128 (got %lld)", (long long)M);
-  if (N % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: N must be divisible by 128 (got %lld)", (long long)N);
-  if (K % 64 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: K must be divisible by 64 (got %lld)", (long long)K);
-  Q2B_REQUIRE_PTR(D);
-  Q2B_REQUIRE_PTR(A);
-  Q2B_REQUIRE_PTR(B);
-  Q2B_REQUIRE_PTR(sfa);
-  Q2B_REQUIRE_PTR(sfb);
-  Q2B_REQUIRE_NONNULL(alpha);
+}  // extern "C"
+
+namespace {
+
+// Output tiles of the 1-SM kernel at BN=128 and the K split that fills the
+// SMs when there are too few of them (decode-sized M).  A split keeps at
+// least two 256-wide K blocks per unit.
+struct SplitPlan {
+  int64_t tiles;
+  int splits;
+};
+
+SplitPlan plan_split(int64_t m_valid, int64_t N, int64_t K, int sms) {
+  const int64_t tiles = ((m_valid + 127) / 128) * (N / 128);
+  const int64_t nkb = (K + 255) / 256;
+  int64_t splits = 1;
+  if (tiles * 2 <= sms) {
+    splits = sms / tiles;
+    if (splits > nkb / 2) splits = nkb / 2;
+    if (splits < 1) splits = 1;
+  }
+  return {tiles, static_cast<int>(splits)};
+}
+
+int64_t split_ws_bytes(const SplitPlan& sp) {
+  if (sp.splits <= 1) return 0;
+  // fp32 tile slabs, then one counter per (tile, epilogue warp)
+  return sp.tiles * 128 * 128 * 4 + sp.tiles * q2b::GemmCfg<128>::kEpiWarps * 4;
+}
+
+int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                int64_t m_valid, int64_t N, int64_t K, void* ws, int64_t ws_bytes, void* stream) {
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t M = (m_valid + 127) / 128 * 128;
   CUtensorMap ta, tb;
   q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha,
-                    static_cast<__nv_bfloat16*>(D)};
-  if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, 128, 128)) return r;
+                    static_cast<__nv_bfloat16*>(D), m_valid, 1, nullptr, nullptr};
+  if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
-  if (M % 256 == 0 && N % 256 == 0 && sms >= 2) {
+  if (m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms) {
     // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair
     CUtensorMap tsa, tsb;
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
@@ -477,23 +512,67 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
     return Q2B_OK;
   }
 #endif
-#ifdef Q2B_GEMM_PROBE_BN128
-  if (false) {
-#else
-  if (N % 256 == 0) {
-#endif
+  const SplitPlan sp = plan_split(m_valid, N, K, sms);
+  const bool split = sp.splits > 1 && ws != nullptr && ws_bytes >= split_ws_bytes(sp);
+  if (N % 256 == 0 && !split && (M / 128) * (N / 256) * 2 >= sms) {
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 256)) return r;
     const int64_t tiles = (M / 128) * (N / 256);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
     q2b::gemm_nvfp4_kernel<256><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
   } else {
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
-    const int64_t tiles = (M / 128) * (N / 128);
-    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    int64_t units = sp.tiles;
+    if (split) {
+      p.splits = sp.splits;
+      p.ws = static_cast<float*>(ws);
+      p.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + sp.tiles * 128 * 128 * 4);
+      units = sp.tiles * sp.splits;
+    }
+    const int grid = static_cast<int>(units < sms ? units : sms);
     q2b::gemm_nvfp4_kernel<128><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
   }
   Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
+}
+
+int check_gemm_args(const char* name, void* D, const void* A, const void* B, const void* sfa, const void* sfb,
+                    const float* alpha, int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(Q2B_ERR_INVALID, "%s: empty problem", name);
+  if (N % 128 != 0) return fail(Q2B_ERR_INVALID, "%s: N must be divisible by 128 (got %lld)", name, (long long)N);
+  if (K % 64 != 0) return fail(Q2B_ERR_INVALID, "%s: K must be divisible by 64 (got %lld)", name, (long long)K);
+  Q2B_REQUIRE_PTR(D);
+  Q2B_REQUIRE_PTR(A);
+  Q2B_REQUIRE_PTR(B);
+  Q2B_REQUIRE_PTR(sfa);
+  Q2B_REQUIRE_PTR(sfb);
+  Q2B_REQUIRE_NONNULL(alpha);
+  return Q2B_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                   int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M > 0 && M % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: M must be divisible by 128 (got %lld)", (long long)M);
+  if (int r = check_gemm_args("fp4_mm", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  return gemm_launch(D, A, B, sfa, sfb, alpha, M, N, K, nullptr, 0, stream);
+}
+
+int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 != 0) return 0;
+  int dev, sms;
+  if (device_setup(&dev, &sms)) return -1;
+  return split_ws_bytes(plan_split(M, N, K, sms));
+}
+
+int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                      int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (int r = check_gemm_args("fp4_mm_ex", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return fail(Q2B_ERR_INVALID, "fp4_mm_ex: workspace must be 16-byte aligned");
+  return gemm_launch(D, A, B, sfa, sfb, alpha, M, N, K, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -59,6 +59,15 @@ int q2b_abs_max(float* out, const void* x, int64_t n, void* stream);
 int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
                   int64_t rows, int64_t cols, int mode, void* stream);
 
+/* q2b_quant_fwd for any rows >= 1 (cols a multiple of 128).  codes are
+ * [rows, cols/2]; sf is the blocked layout of ceil(rows/128)*128 rows, of
+ * which only the rows that exist are written (the caller zero-fills the
+ * rest once).  Serves the inference linear without padding its input.
+ * Replaces: the 128-row F.pad + four_six_fp4 of QuartetIILinearMethod.apply,
+ * src/evals/vllm_plugin/quartet2_quant.py:110-128. */
+int q2b_quant_fwd_ragged(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
+                         int64_t rows, int64_t cols, int mode, void* stream);
+
 /* Rotation by the 128-point randomized Hadamard transform (h: h_rows = 16,
  * the top slice, extended by Sylvester's construction and row-swizzled as
  * quartet2/python/quartet2/rht.py:65-82) or by an explicit 128x128 matrix
@@ -122,6 +131,25 @@ int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* s
  * quartet2/python/quartet2/linear.py:34-56. */
 int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                    int64_t M, int64_t N, int64_t K, void* stream);
+
+/* q2b_gemm_nvfp4 for any M >= 1 (N a multiple of 128, K of 64).  A is
+ * [M, K/2] (rows past M are read as zero), sfa the blocked scales of
+ * ceil(M/128)*128 rows, D [M, N] (only rows < M are written).  When the
+ * output has too few 128x128 tiles to fill the GPU (decode-sized M), K is
+ * split across CTAs and the partial tiles are summed in fp32 in `workspace`
+ * (q2b_gemm_workspace_bytes(M, N, K) bytes, 16-byte aligned, zero-filled
+ * once by the caller; every call leaves it zero again).  With a smaller or
+ * null workspace the call runs unsplit.  Calls that share a workspace must
+ * not overlap on the GPU.
+ * Replaces: the padded _fp4_mm of QuartetIILinearMethod.apply and its row
+ * slice, src/evals/vllm_plugin/quartet2_quant.py:125-137. */
+int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                      int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes q2b_gemm_nvfp4_ex uses for this shape on the current
+ * device (0 = it never splits K); -1 if no device is usable.
+ * No counterpart in the reference (its GEMM library manages its own). */
+int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 #ifdef __cplusplus
 }

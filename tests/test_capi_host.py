@@ -15,7 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_symbols():
     text = open(os.path.join(ROOT, "include", "q2b.h")).read()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(q2b_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^(?:int|int64_t|const char\*)\s+(q2b_\w+)\(", text, re.M)))
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -66,6 +66,20 @@ def test_gemm_rejects_bad_shapes():
         _lib.call("q2b_gemm_nvfp4", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100, 128, 128, None)
     with pytest.raises(ValueError, match="K must be divisible by 64"):
         _lib.call("q2b_gemm_nvfp4", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 128, 128, 80, None)
+
+
+def test_ragged_entry_points_reject_bad_arguments():
+    with pytest.raises(ValueError, match="rows must be positive"):
+        _lib.call("q2b_quant_fwd_ragged", FAKE, FAKE, FAKE, FAKE, FAKE, 1.0, 0, 128, 1, None)
+    with pytest.raises(ValueError, match="cols must be divisible by 128"):
+        _lib.call("q2b_quant_fwd_ragged", FAKE, FAKE, FAKE, FAKE, FAKE, 1.0, 3, 200, 1, None)
+    with pytest.raises(ValueError, match="N must be divisible by 128"):
+        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 100, 128, None, 0, None)
+    with pytest.raises(ValueError, match="workspace must be 16-byte aligned"):
+        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 128, 128, ctypes.c_void_p(0x10004),
+                  64, None)
+    # no split plan for a shape the GEMM rejects
+    assert _lib.load().q2b_gemm_workspace_bytes(1, 100, 128) == 0
 
 
 def test_last_error_is_thread_local_text():
