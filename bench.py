@@ -41,9 +41,9 @@ KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2
                     "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1}
 
 
-# Average DRAM bytes (read + write) per gemm_nvfp4_kernel launch over one step of this workload,
+# Average DRAM bytes (read + write) per gemm_nvfp4_2sm_kernel launch over one step of this workload,
 # from the ncu launch list summarised in profiles/step_launches_4b_linear_set.txt.
-GEMM_DRAM_BYTES_PER_LAUNCH = 1843.1e6
+GEMM_DRAM_BYTES_PER_LAUNCH = 1667.9e6
 
 
 def flops_per_token() -> float:
@@ -290,11 +290,27 @@ def run_ours(args) -> None:
     res_host = torch.empty(len(layers), dtype=torch.float32).pin_memory()
     d2h = res_host.numel() * res_host.element_size()
 
+    copy_stream = torch.cuda.Stream(dev)
+
     def e2e_step():
+        # every layer's inputs go host -> device on a copy stream, issued up front, so the
+        # PCIe transfers of later layers overlap the compute of earlier ones
+        cur = torch.cuda.current_stream(dev)
+        copy_stream.wait_stream(cur)
+        staged = []
+        with torch.cuda.stream(copy_stream):
+            for hx, hdy in zip(host_x, host_dy):
+                x = hx.to(dev, non_blocking=True)
+                dy = hdy.to(dev, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                staged.append((x, dy, ev))
         norms = []
-        for lay, hx, hdy in zip(layers, host_x, host_dy):
-            x = hx.to(dev, non_blocking=True).requires_grad_(True)
-            dy = hdy.to(dev, non_blocking=True)
+        for lay, (x, dy, ev) in zip(layers, staged):
+            cur.wait_event(ev)
+            x.record_stream(cur)
+            dy.record_stream(cur)
+            x.requires_grad_(True)
             lay.weight.grad = None
             y = lay(x.view(1, M, -1))
             y.backward(dy.view(1, M, -1))
@@ -341,8 +357,9 @@ def run_ours(args) -> None:
         "e2e": {"value": world * flops_step / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "Quartet_II_linear API; activations and output gradients copied from pinned host "
-                        "memory each step, weight-gradient norms read back"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_nvfp4_kernel", "achieved": achieved,
+                        "memory each step (on a copy stream, overlapping earlier layers' compute), "
+                        "weight-gradient norms read back"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_nvfp4_2sm_kernel", "achieved": achieved,
                      "peak": fp4_peak, "unit": "TFLOP/s",
                      "frac": (achieved / fp4_peak) if achieved else None,
                      "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
@@ -355,12 +372,79 @@ def run_ours(args) -> None:
         "clocks": clocks,
         "lib": _lib.lib_path(),
     }
+    if world == 1 and not args.no_small_m:
+        line["small_m"] = small_m_report(dev)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_entry(cpu_step_tokens())
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+SMALL_M = [1, 8, 64, 256, 4096]
+
+
+def small_m_report(dev, reps: int = 200) -> dict:
+    """forward-only inference linears with pre-quantized weights at decode and
+    prefill M, through cloverlm_b200.inference.apply (no row padding, split-K at small M).  Each call
+    is captured in a CUDA graph (as vLLM runs decode) and replayed `reps` times; the time per call is
+    device time from CUDA events.  `padded_us` is the reference's algorithm (rows padded to 128,
+    quantized, multiplied and sliced) on the same kernels, captured the same way."""
+    import torch
+    import torch.nn.functional as F
+
+    from cloverlm_b200 import inference
+    from cloverlm_b200.linear import _fp4_mm
+    from cloverlm_b200.quant import NVFP4QuantMode, abs_max, quant_fp4
+
+    def graph_time(fn):
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):  # same stream as the warm-up: reuses its split-K workspace
+            fn()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    out = {"unit": "us per call (CUDA graph replay, device time)", "reps": reps,
+           "config": "BASELINE config 5: W pre-quantized four-over-six from N(0,0.02), X ~ N(0,1) bf16",
+           "shapes": {}}
+    gen = torch.Generator(device=dev).manual_seed(7)
+    for name, K, N in SHAPES:
+        w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        prep = inference.prepare_weight(w)
+        rows = {}
+        for m in SMALL_M:
+            x = torch.randn(m, K, device=dev, generator=gen).to(torch.bfloat16)
+
+            def ours():
+                return inference.apply(prep, x)
+
+            def padded():
+                xp = F.pad(x, (0, 0, 0, (-m) % 128))
+                q = quant_fp4(xp, amax=abs_max(xp), scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+                return _fp4_mm(q.fp4, prep.fp4, q.micro_scales, prep.micro_scales,
+                               q.tensor_scale * prep.tensor_scale)[:m]
+
+            t_ours = graph_time(ours)
+            t_pad = graph_time(padded)
+            rows[str(m)] = {"ours_us": round(t_ours, 2), "padded_us": round(t_pad, 2),
+                            "tflops": round(2.0 * m * N * K / (t_ours * 1e-6) / 1e12, 2)}
+        out["shapes"][f"{name} {K}->{N}"] = rows
+    return out
 
 
 def main():
@@ -371,6 +455,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=65536)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-small-m", action="store_true", help="skip the inference-linear latency section")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
