@@ -30,6 +30,7 @@ struct GemmParams {
   const uint8_t* sfa;   // blocked [M, K/16]
   const uint8_t* sfb;   // blocked [N, K/16]
   const float* alpha;
+  const float* alpha_b; // optional second factor of alpha (nullptr = 1)
   __nv_bfloat16* D;     // [m_valid, N] row-major
   int64_t m_valid;      // rows of A and D that exist (A rows past it read as zero through TMA)
   int splits;           // K split into this many ranges per output tile (1 = none)
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter
     constexpr int kColsPerWarp = BN / 2;
     const int c0 = (e >> 2) * kColsPerWarp;
-    const float alpha = *p.alpha;
+    const float alpha = *p.alpha * (p.alpha_b != nullptr ? *p.alpha_b : 1.f);
     int64_t tc = 0;
     for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x, ++tc) {
       const int buf = static_cast<int>(tc % Cfg::kAccBufs);
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     const int q = warp & 3;
     constexpr int kCols = 256 / (Cfg::kEpiWarps / 4);  // columns per warp
     const int c0 = (e >> 2) * kCols;
-    const float alpha = *p.alpha;
+    const float alpha = *p.alpha * (p.alpha_b != nullptr ? *p.alpha_b : 1.f);
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {

@@ -251,6 +251,48 @@ int q2b_quant_fwd_ragged(void* codes, void* sf, float* ts, const void* x, const 
   return quant_fwd_impl(codes, sf, ts, x, amax, scale_override, rows, cols, mode, stream, true);
 }
 
+int q2b_quant_rows_fused(void* codes, void* sf, float* ts, const void* x, float scale_override, int64_t rows,
+                         int64_t cols, int mode, void* stream) {
+  if (mode != Q2B_MODE_RNE && mode != Q2B_MODE_FOUR_SIX)
+    return fail(Q2B_ERR_INVALID, "quant_rows_fused: unknown mode %d", mode);
+  if (cols <= 0 || cols % 128 != 0) return fail(Q2B_ERR_INVALID, "quant_rows_fused: cols must be divisible by 128");
+  if (rows <= 0) return fail(Q2B_ERR_INVALID, "quant_rows_fused: rows must be positive");
+  Q2B_REQUIRE_PTR(codes);
+  Q2B_REQUIRE_PTR(sf);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(ts);
+  if ((reinterpret_cast<uintptr_t>(x) & 31u) != 0)
+    return fail(Q2B_ERR_INVALID, "Pointer `x` is not aligned to 32 bytes");
+  const int64_t ngroups = rows * cols / 16;
+  if (ngroups >= (int64_t(1) << 31)) return fail(Q2B_ERR_INVALID, "quant_rows_fused: tensor too large");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  const uint32_t gpr = static_cast<uint32_t>(cols / 16);
+  const uint64_t magic = ~uint64_t(0) / gpr + 1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = q2b::kRowsClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(q2b::kRowsClusterCtas, 1, 1);
+  cfg.blockDim = dim3(q2b::kRowsThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto* c = static_cast<uint2*>(codes);
+  auto* s = static_cast<uint8_t*>(sf);
+  auto* xx = static_cast<const uint16_t*>(x);
+  if (mode == Q2B_MODE_FOUR_SIX)
+    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::quant_rows_cluster_kernel<true>, c, s, ts, xx, scale_override,
+                                static_cast<uint32_t>(rows), static_cast<uint32_t>(ngroups), gpr, magic));
+  else
+    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::quant_rows_cluster_kernel<false>, c, s, ts, xx, scale_override,
+                                static_cast<uint32_t>(rows), static_cast<uint32_t>(ngroups), gpr, magic));
+  return Q2B_OK;
+}
+
 int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scratch_max, const void* h, int h_rows,
                  const void* x, uint64_t seed, float fp4_max, float fp8_max, int64_t M, int64_t N, int transpose,
                  void* stream) {
@@ -474,13 +516,14 @@ int64_t split_ws_bytes(const SplitPlan& sp) {
 }
 
 int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
-                int64_t m_valid, int64_t N, int64_t K, void* ws, int64_t ws_bytes, void* stream) {
+                const float* alpha_b, int64_t m_valid, int64_t N, int64_t K, void* ws, int64_t ws_bytes,
+                void* stream) {
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t M = (m_valid + 127) / 128 * 128;
   CUtensorMap ta, tb;
-  q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha,
+  q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha, alpha_b,
                     static_cast<__nv_bfloat16*>(D), m_valid, 1, nullptr, nullptr};
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
@@ -557,7 +600,7 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
                    int64_t M, int64_t N, int64_t K, void* stream) {
   if (M > 0 && M % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: M must be divisible by 128 (got %lld)", (long long)M);
   if (int r = check_gemm_args("fp4_mm", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
-  return gemm_launch(D, A, B, sfa, sfb, alpha, M, N, K, nullptr, 0, stream);
+  return gemm_launch(D, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream);
 }
 
 int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
@@ -568,11 +611,12 @@ int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 }
 
 int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
-                      int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream) {
+                      const float* alpha_b, int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                      void* stream) {
   if (int r = check_gemm_args("fp4_mm_ex", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
   if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
     return fail(Q2B_ERR_INVALID, "fp4_mm_ex: workspace must be 16-byte aligned");
-  return gemm_launch(D, A, B, sfa, sfb, alpha, M, N, K, workspace, workspace_bytes, stream);
+  return gemm_launch(D, A, B, sfa, sfb, alpha, alpha_b, M, N, K, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -99,9 +99,13 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
   const int lane = threadIdx.x & 31;
   const uint32_t stride = gridDim.x * blockDim.x;
   const uint32_t n_kt = gpr >> 2;
-  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
-    uint32_t w[8];
-    ldg256(x + static_cast<uint64_t>(g) * 16, w);
+  // whole warps stay in the loop (the scale gather below shuffles across the
+  // warp); lanes past the end load nothing and store nothing
+  const uint32_t ngroups_up = (ngroups + 31u) & ~31u;
+  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < ngroups_up; g += stride) {
+    const bool valid = g < ngroups;
+    uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
     float xs[16], xa[16], m[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -124,17 +128,124 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
       const float e4 = quant16(xs, xa, gabs, inv4, inv_ts, tab, c4, s4);
       if (e4 < e6) { c = c4; s = s4; }
     }
-    __stcs(codes + g, c);
+    if (valid) __stcs(codes + g, c);
     const uint32_t b1 = __shfl_down_sync(0xffffffffu, s, 1);
     const uint32_t b2 = __shfl_down_sync(0xffffffffu, s, 2);
     const uint32_t b3 = __shfl_down_sync(0xffffffffu, s, 3);
-    if ((lane & 3) == 0) {
+    if (valid && (lane & 3) == 0) {
       const uint32_t row = static_cast<uint32_t>(__umul64hi(static_cast<uint64_t>(g), gpr_magic));
       const uint32_t kb = g - row * gpr;
       const uint64_t off = ((static_cast<uint64_t>(row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) |
                            (((row >> 5) & 3) << 2);
       *reinterpret_cast<uint32_t*>(sf + off) = s | (b1 << 8) | (b2 << 16) | (b3 << 24);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Small-input path of the inference linear: abs-max, tensor scale and
+// four-over-six (or RNE) quantization of x [rows, cols] in ONE launch of a
+// single thread-block cluster.  Each CTA reduces the abs-max of its share of
+// the groups, the CTAs exchange their maxima through distributed shared
+// memory, and every CTA then quantizes its share exactly as
+// quant_fwd_v2_kernel does.  Scale words of the padding rows of the last
+// 128-row block (rows..ceil(rows/128)*128-1) are written as zero.
+constexpr int kRowsClusterCtas = 8;
+constexpr int kRowsThreads = 512;
+
+template <bool kFourSix>
+__global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
+    uint2* __restrict__ codes, uint8_t* __restrict__ sf, float* __restrict__ ts_out, const uint16_t* __restrict__ x,
+    float scale_override, uint32_t rows, uint32_t ngroups, uint32_t gpr, uint64_t gpr_magic) {
+  __shared__ QuantTables tab;
+  __shared__ float red[kRowsThreads / 32];
+  __shared__ float cta_max;
+  const uint32_t rank = cluster_ctarank();
+  const int lane = threadIdx.x & 31;
+  const uint32_t stride = kRowsClusterCtas * kRowsThreads;
+  const uint32_t first = rank * kRowsThreads + threadIdx.x;
+
+  // phase 1: abs-max of this CTA's groups
+  float m = 0.f;
+  for (uint32_t g = first; g < ngroups; g += stride) {
+    uint32_t w[8];
+    ldg256(x + static_cast<uint64_t>(g) * 16, w);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = fmaxf(m, fmaxf(fabsf(bf16lo(w[k])), fabsf(bf16hi(w[k]))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < kRowsThreads / 32; ++k) m = fmaxf(m, red[k]);
+    cta_max = m;
+  }
+  cluster_sync();  // every CTA's cta_max is written
+  float amax = 0.f;
+#pragma unroll
+  for (int r = 0; r < kRowsClusterCtas; ++r) amax = fmaxf(amax, ld_shared_cluster_f32(map_to_rank(smem_u32(&cta_max), r)));
+  cluster_sync();  // no CTA leaves (or reuses cta_max) while another still reads it
+
+  // phase 2: quantization, as quant_fwd_v2_kernel
+  const float inv_scales_max = kFourSix ? 1.f / 256.f : 1.f / 448.f;
+  const float inv_val_max = scale_override * (1.f / 6.f);
+  const float ts = (amax == 0.f) ? 1.f : amax * inv_scales_max * inv_val_max;
+  if (rank == 0 && threadIdx.x == 0) *ts_out = ts;
+  fill_quant_tables(tab, ts);
+  __syncthreads();
+  const float inv_ts = rcp_rn(ts);
+  const float inv6 = (1.f / 6.f) * scale_override;
+  const float inv4 = (1.f / 4.f) * scale_override;
+  const uint32_t n_kt = gpr >> 2;
+  // whole warps stay in the loop (the scale gather shuffles across the warp)
+  const uint32_t ngroups_up = (ngroups + 31u) & ~31u;
+  for (uint32_t g = first; g < ngroups_up; g += stride) {
+    const bool valid = g < ngroups;
+    uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
+    float xs[16], xa[16], mm[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      xs[2 * k] = bf16lo(w[k]);
+      xs[2 * k + 1] = bf16hi(w[k]);
+      const uint32_t a = w[k] & 0x7FFF7FFFu;
+      xa[2 * k] = bf16lo(a);
+      xa[2 * k + 1] = bf16hi(a);
+      mm[k] = fmaxf(xa[2 * k], xa[2 * k + 1]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mm[k] = fmaxf(mm[k], mm[k + 4]);
+    const float gabs = fmaxf(fmaxf(mm[0], mm[2]), fmaxf(mm[1], mm[3]));
+    uint2 c;
+    uint32_t sc;
+    const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, sc);
+    if constexpr (kFourSix) {
+      uint2 c4;
+      uint32_t s4;
+      const float e4 = quant16(xs, xa, gabs, inv4, inv_ts, tab, c4, s4);
+      if (e4 < e6) { c = c4; sc = s4; }
+    }
+    if (valid) codes[g] = c;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, sc, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, sc, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, sc, 3);
+    if (valid && (lane & 3) == 0) {
+      const uint32_t row = static_cast<uint32_t>(__umul64hi(static_cast<uint64_t>(g), gpr_magic));
+      const uint32_t kb = g - row * gpr;
+      const uint64_t off = ((static_cast<uint64_t>(row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) |
+                           (((row >> 5) & 3) << 2);
+      *reinterpret_cast<uint32_t*>(sf + off) = sc | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+  }
+  // zero scale words of the padding rows (one 32-bit word = 4 groups of a row)
+  const uint32_t rows_pad = (rows + 127) & ~127u;
+  const uint32_t pad_words = (rows_pad - rows) * n_kt;
+  for (uint32_t i = first; i < pad_words; i += stride) {
+    const uint32_t row = rows + i / n_kt, kt = i % n_kt;
+    const uint64_t off = ((static_cast<uint64_t>(row >> 7) * n_kt + kt) << 9) | ((row & 31) << 4) |
+                         (((row >> 5) & 3) << 2);
+    *reinterpret_cast<uint32_t*>(sf + off) = 0u;
   }
 }
 

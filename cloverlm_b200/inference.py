@@ -10,7 +10,10 @@ that pad ``out_features`` to a multiple of 128 (quartet2_quant.py:80-99).
 the reference pads them to a multiple of 128 with ``F.pad``, quantizes and
 multiplies the padded matrix and slices the output (quartet2_quant.py:110-137).
 Here the activations are quantized and multiplied as they are
-(``q2b_quant_fwd_ragged``, ``q2b_gemm_nvfp4_ex``): the GEMM reads rows past M
+(``q2b_quant_rows_fused`` -- abs-max, scale and codes in one launch -- for
+decode-sized inputs, ``q2b_abs_max`` + ``q2b_quant_fwd_ragged`` for larger
+ones, then ``q2b_gemm_nvfp4_ex`` with both tensor scales passed as pointers,
+so no product kernel runs): the GEMM reads rows past M
 as zeros through its TMA descriptor and stores only rows < M, and at
 decode-sized M it splits K across the SMs and sums the partial tiles in fp32.
 The codes and scales of the real rows are the ones the padded path produces
@@ -69,6 +72,12 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor |
         return ws
 
 
+# Inputs up to this many 16-element groups are quantized by the one-launch
+# cluster kernel (abs-max, scale and codes together); larger ones by the
+# grid-wide abs-max and quantizer kernels.
+FUSED_MAX_GROUPS = 1 << 14
+
+
 def quant_rows(x: torch.Tensor, amax: torch.Tensor | None = None):
     """Four-over-six quantization of bf16 x [M, K] for any M >= 1.
 
@@ -77,34 +86,42 @@ def quant_rows(x: torch.Tensor, amax: torch.Tensor | None = None):
     assert x.dtype == torch.bfloat16 and x.is_cuda and x.dim() == 2
     x = x.contiguous()
     m, k = x.shape
-    if amax is None:
-        amax = abs_max(x)
     m_pad = (m + 127) // 128 * 128
     codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
-    scales = torch.zeros((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
     ts = torch.empty((), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
+        if amax is None and m * k // 16 <= FUSED_MAX_GROUPS:
+            scales = torch.empty((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
+            _lib.call("q2b_quant_rows_fused", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x), 1.0,
+                      m, k, _lib.MODE_FOUR_SIX, _lib.stream_of(x))
+            return codes, scales, ts
+        if amax is None:
+            amax = abs_max(x)
+        scales = torch.zeros((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
         _lib.call("q2b_quant_fwd_ragged", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x),
                   _lib.ptr(amax), 1.0, m, k, _lib.MODE_FOUR_SIX, _lib.stream_of(x))
     return codes, scales, ts
 
 
 def fp4_mm_rows(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_mx: torch.Tensor,
-                alpha: torch.Tensor) -> torch.Tensor:
-    """bf16 [M, N] = alpha * dq(x) @ dq(w)^T for any M >= 1 (x_mx padded to whole 128-row blocks)."""
+                alpha: torch.Tensor, alpha_b: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [M, N] = alpha (* alpha_b) * dq(x) @ dq(w)^T for any M >= 1 (x_mx padded to whole 128-row blocks)."""
     m, packed_k = x_fp4.shape
     k = packed_k * 2
     n = w_fp4.shape[0]
     out = torch.empty((m, n), dtype=torch.bfloat16, device=x_fp4.device)
     if alpha.dtype != torch.float32:
         alpha = alpha.float()
+    if alpha_b is not None and alpha_b.dtype != torch.float32:
+        alpha_b = alpha_b.float()
     with torch.cuda.device(x_fp4.device):
         lib = _lib.load()
         nbytes = int(lib.q2b_gemm_workspace_bytes(m, n, k))
         stream = _lib.stream_of(x_fp4)
         ws = _workspace(x_fp4.device, stream.value, nbytes)
         _lib.call("q2b_gemm_nvfp4_ex", _lib.ptr(out), _lib.ptr(x_fp4), _lib.ptr(w_fp4), _lib.ptr(x_mx),
-                  _lib.ptr(w_mx), _lib.ptr(alpha), m, n, k, _lib.ptr(ws), nbytes if ws is not None else 0, stream)
+                  _lib.ptr(w_mx), _lib.ptr(alpha), _lib.ptr(alpha_b), m, n, k, _lib.ptr(ws),
+                  nbytes if ws is not None else 0, stream)
     return out
 
 
@@ -115,7 +132,7 @@ def apply(prepared: PreparedWeight, x: torch.Tensor, bias: torch.Tensor | None =
     if flat.dtype != torch.bfloat16:
         flat = flat.to(torch.bfloat16)
     codes, scales, ts = quant_rows(flat)
-    out = fp4_mm_rows(codes, prepared.fp4, scales, prepared.micro_scales, ts * prepared.tensor_scale)
+    out = fp4_mm_rows(codes, prepared.fp4, scales, prepared.micro_scales, ts, prepared.tensor_scale)
     if prepared.w_pad:
         out = out[:, :prepared.out_features]
     out = out.reshape(*orig_shape[:-1], out.shape[-1])

@@ -68,6 +68,17 @@ int q2b_quant_fwd(void* codes, void* sf, float* ts, const void* x, const float* 
 int q2b_quant_fwd_ragged(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
                          int64_t rows, int64_t cols, int mode, void* stream);
 
+/* Abs-max, tensor scale and quantization of x [rows, cols] in one launch (a
+ * single cluster of 8 CTAs that exchange their partial maxima through
+ * distributed shared memory), with the scale words of the padding rows of
+ * the last 128-row block written as zero: the caller needs no amax buffer and
+ * no zero-fill.  For small inputs (decode-sized rows); large ones are faster
+ * through q2b_abs_max + q2b_quant_fwd_ragged.  Outputs as q2b_quant_fwd_ragged.
+ * Replaces: abs_max + F.pad + four_six_fp4 of QuartetIILinearMethod.apply,
+ * src/evals/vllm_plugin/quartet2_quant.py:110-128. */
+int q2b_quant_rows_fused(void* codes, void* sf, float* ts, const void* x, float scale_override, int64_t rows,
+                         int64_t cols, int mode, void* stream);
+
 /* Rotation by the 128-point randomized Hadamard transform (h: h_rows = 16,
  * the top slice, extended by Sylvester's construction and row-swizzled as
  * quartet2/python/quartet2/rht.py:65-82) or by an explicit 128x128 matrix
@@ -132,7 +143,9 @@ int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* s
 int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                    int64_t M, int64_t N, int64_t K, void* stream);
 
-/* q2b_gemm_nvfp4 for any M >= 1 (N a multiple of 128, K of 64).  A is
+/* q2b_gemm_nvfp4 for any M >= 1 (N a multiple of 128, K of 64), scaled by
+ * *alpha times *alpha_b when alpha_b is not null (the two tensor scales,
+ * so no separate product kernel runs).  A is
  * [M, K/2] (rows past M are read as zero), sfa the blocked scales of
  * ceil(M/128)*128 rows, D [M, N] (only rows < M are written).  When the
  * output has too few 128x128 tiles to fill the GPU (decode-sized M), K is
@@ -144,7 +157,8 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
  * Replaces: the padded _fp4_mm of QuartetIILinearMethod.apply and its row
  * slice, src/evals/vllm_plugin/quartet2_quant.py:125-137. */
 int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
-                      int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream);
+                      const float* alpha_b, int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                      void* stream);
 
 /* Workspace bytes q2b_gemm_nvfp4_ex uses for this shape on the current
  * device (0 = it never splits K); -1 if no device is usable.

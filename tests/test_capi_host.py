@@ -74,10 +74,14 @@ def test_ragged_entry_points_reject_bad_arguments():
     with pytest.raises(ValueError, match="cols must be divisible by 128"):
         _lib.call("q2b_quant_fwd_ragged", FAKE, FAKE, FAKE, FAKE, FAKE, 1.0, 3, 200, 1, None)
     with pytest.raises(ValueError, match="N must be divisible by 128"):
-        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 100, 128, None, 0, None)
+        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, 1, 100, 128, None, 0, None)
     with pytest.raises(ValueError, match="workspace must be 16-byte aligned"):
-        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 128, 128, ctypes.c_void_p(0x10004),
+        _lib.call("q2b_gemm_nvfp4_ex", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, 1, 128, 128, ctypes.c_void_p(0x10004),
                   64, None)
+    with pytest.raises(ValueError, match="rows must be positive"):
+        _lib.call("q2b_quant_rows_fused", FAKE, FAKE, FAKE, FAKE, 1.0, 0, 128, 1, None)
+    with pytest.raises(ValueError, match="unknown mode"):
+        _lib.call("q2b_quant_rows_fused", FAKE, FAKE, FAKE, FAKE, 1.0, 1, 128, 5, None)
     # no split plan for a shape the GEMM rejects
     assert _lib.load().q2b_gemm_workspace_bytes(1, 100, 128) == 0
 

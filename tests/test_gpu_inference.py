@@ -58,6 +58,35 @@ def test_ragged_quant_matches_padded_rows(m):
     assert ts.item() == q.tensor_scale.item()
 
 
+@pytest.mark.parametrize("m,k", [(1, 128), (3, 256), (2, 384), (130, 128), (64, 14336), (700, 3584)])
+@pytest.mark.parametrize("path", ["fused", "two_kernel"])
+def test_ragged_quant_both_paths_match_padded_rows(m, k, path):
+    """The one-launch cluster path (abs-max + codes) and the abs-max + ragged-quantizer path, on
+    row counts and widths whose group counts are not multiples of a warp."""
+    x, _ = _inputs(m, k, 128, seed=m * 7 + k)
+    codes, scales, ts = quant_rows(x) if path == "fused" else quant_rows(x, amax=abs_max(x))
+    xp = F.pad(x, (0, 0, 0, (-m) % 128))
+    q = quant_fp4(xp, amax=abs_max(xp), scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    assert torch.equal(codes, q.fp4[:m])
+    assert torch.equal(scales.view(torch.uint8), q.micro_scales.view(torch.uint8))
+    assert ts.item() == q.tensor_scale.item()
+
+
+def test_fused_rows_rne_mode_matches_quant_fp4():
+    m, k = 9, 640
+    x, _ = _inputs(m, k, 128, seed=3)
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device="cuda")
+    scales = torch.full((128 * k // 16,), 0xFF, dtype=torch.uint8, device="cuda")  # pad rows must come back 0
+    ts = torch.empty((), device="cuda")
+    _lib.call("q2b_quant_rows_fused", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x), 1.0, m, k,
+              _lib.MODE_RNE, _lib.stream_of(x))
+    xp = F.pad(x, (0, 0, 0, 128 - m))
+    q = quant_fp4(xp, amax=abs_max(xp), scale_override=1.0, mode=NVFP4QuantMode.RNE)
+    assert torch.equal(codes, q.fp4[:m])
+    assert torch.equal(scales, q.micro_scales.view(torch.uint8).reshape(-1))
+    assert ts.item() == q.tensor_scale.item()
+
+
 @pytest.mark.parametrize("m,k,n", [(1, 3584, 3584), (8, 3584, 10752), (64, 14336, 3584), (1, 512, 384),
                                    (37, 1024, 640), (256, 3584, 3584), (300, 512, 256), (4096, 3584, 3584)])
 def test_apply_matches_padded_path_and_fp32(m, k, n):
