@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   uint64_t* sfready = empty + Cfg::kStages;
   uint64_t* tfull = sfready + Cfg::kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;  // every tcgen05 issuer's final commit: nothing in flight at dealloc
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles_n = p.N / BN;
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], Cfg::kEpiWarps);
     }
+    mbar_init(drain, 1 + Cfg::kSfWarps);
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
@@ -197,6 +199,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
       }
+      tc_commit(drain);
+      mbar_wait(drain, 0, kTimeoutProducer);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
@@ -241,6 +245,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
         if (!ok) break;
         tc_commit(&tfull[buf]);
       }
+      tc_commit(drain);
+      mbar_wait(drain, 0, kTimeoutProducer);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -429,7 +435,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   uint64_t* sfready = empty + Cfg::kStages;
   uint64_t* tfull = sfready + Cfg::kStages;
   uint64_t* tempty = tfull + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 1);
+  uint64_t* drain = tempty + 1;  // leader's tcgen05 issuers' final commits: nothing in flight at dealloc
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #ifdef Q2B_GEMM_PROBE_TIMING
@@ -460,6 +467,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * Cfg::kEpiWarps);
+    mbar_init(drain, 1 + Cfg::kSfWarps);
     fence_barrier_init();
   }
   if (threadIdx.x == 32) {
@@ -549,6 +557,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         }
         tc_commit_pair_leader(&sfready[slot]);
       }
+      tc_commit_pair_leader(drain);
+      mbar_wait(drain, 0, kTimeoutProducer);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue (leader, lane 0)
@@ -571,11 +581,9 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
 #endif
         tc_fence_after();
         for (int64_t kb = 0; kb < nkb; ++kb) {
-#ifndef Q2B_GEMM_PROBE_NO_SFWAIT
           Q2B_T0
           if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
           Q2B_TW
-#endif
 #ifdef Q2B_GEMM_PROBE_TIMING
           vt_mma[slot] = clock64();
 #endif
@@ -592,6 +600,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         if (!ok) break;
         tc_commit_pair(tfull);
       }
+      tc_commit_pair_leader(drain);
+      mbar_wait(drain, 0, kTimeoutProducer);
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)

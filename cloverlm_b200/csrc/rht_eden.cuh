@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   uint64_t* empty = full + kRhtStages;
   uint64_t* tfull = empty + kRhtStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;  // the MMA warp's final commit: no MMA in flight at dealloc
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles_n = p.N >> 7;
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], Cfg::kEpiWarps);
     }
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (kIn == kInBf16 && threadIdx.x == 0) prefetch_tmap(&tmap_x);
@@ -302,6 +304,11 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       }
       __syncwarp();
     }
+    if (lane == 0) {
+      tc_commit(drain);
+      mbar_wait(drain, 0, kTimeoutProducer);
+    }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
     const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
