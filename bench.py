@@ -215,7 +215,7 @@ def run_ours(args) -> None:
     comm = None
     if world > 1:
         from cloverlm_b200.ddp import GradAllReduce
-        comm = GradAllReduce([lay.weight for lay in layers])
+        comm = GradAllReduce([lay.weight for lay in layers], mode=os.environ.get("Q2B_DDP_MODE", "overlap"))
 
     # bench-only instrumentation: kernel launches and GEMM launch durations
     counters = {"launches": 0, "gemm_events": [], "gemm_bytes": 0.0}
@@ -352,7 +352,8 @@ def run_ours(args) -> None:
         "config": {"workload": "4B Quartet-II linear set fwd+bwd: QKV 3584->10752, O 3584->3584, "
                                "up 3584->14336, down 14336->3584 (BASELINE config 3)",
                    "tokens_per_gpu": M, "tokens_per_s": world * M / (ms / 1e3),
-                   "parallelism": f"dp{world}", "allreduce": "bf16 NCCL AVG" if world > 1 else None,
+                   "parallelism": f"dp{world}",
+                   "allreduce": (f"bf16 NCCL AVG ({comm.mode})" if comm is not None else None),
                    "l2": "inputs larger than L2 (>= 470 MB per operand)"},
         "e2e": {"value": world * flops_step / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

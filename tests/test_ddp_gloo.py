@@ -24,12 +24,12 @@ def _init(rank, world, port, timeout_s=60):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
 
 
-def _worker_average(rank, world, port, q):
+def _worker_average(rank, world, port, q, mode):
     from cloverlm_b200.ddp import GradAllReduce
     _init(rank, world, port)
     torch.manual_seed(0)
     layers = [torch.nn.Linear(8, 4, bias=False).to(torch.bfloat16) for _ in range(3)]
-    comm = GradAllReduce([l.weight for l in layers])
+    comm = GradAllReduce([l.weight for l in layers], mode=mode)
     for step in range(2):
         for l in layers:
             l.weight.grad = None
@@ -56,11 +56,12 @@ def _local_grads(rank, step):
     return out
 
 
-def test_grad_allreduce_averages_across_ranks():
+@pytest.mark.parametrize("mode", ["overlap", "flat"])
+def test_grad_allreduce_averages_across_ranks(mode):
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker_average, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker_average, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world * 2)]
