@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -13,6 +14,7 @@
 #include "gemm_nvfp4.cuh"
 #include "quant_fwd.cuh"
 #include "rht_eden.cuh"
+#include "optim.cuh"
 
 namespace {
 
@@ -197,6 +199,47 @@ int q2b_abs_max(float* out, const void* x, int64_t n, void* stream) {
   const int blocks = static_cast<int>(want < 1 ? 1 : (want < int64_t(sms) * 8 ? want : int64_t(sms) * 8));
   q2b::abs_max_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<unsigned*>(out), static_cast<const uint4*>(x), nvec,
                                               static_cast<const uint16_t*>(x) + nvec * 8, n - nvec * 8);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad, int grad_bf16, int64_t n,
+                   float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step, void* w_bf16,
+                   float* amax, void* stream) {
+  Q2B_REQUIRE_NONNULL(w);
+  Q2B_REQUIRE_NONNULL(exp_avg);
+  Q2B_REQUIRE_NONNULL(exp_avg_sq);
+  Q2B_REQUIRE_NONNULL(grad);
+  if (n <= 0) return fail(Q2B_ERR_INVALID, "adamw: n must be positive");
+  if (step < 1) return fail(Q2B_ERR_INVALID, "adamw: step must be >= 1 (got %lld)", (long long)step);
+  if (!(beta1 >= 0.f && beta1 < 1.f) || !(beta2 >= 0.f && beta2 < 1.f))
+    return fail(Q2B_ERR_INVALID, "adamw: betas must lie in [0, 1)");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  q2b::AdamParams a;
+  const double bc1 = 1.0 - std::pow(static_cast<double>(beta1), static_cast<double>(step));
+  const double bc2 = 1.0 - std::pow(static_cast<double>(beta2), static_cast<double>(step));
+  a.lr_wd = lr * weight_decay;
+  a.beta1 = beta1;
+  a.one_minus_beta1 = 1.f - beta1;
+  a.beta2 = beta2;
+  a.one_minus_beta2 = 1.f - beta2;
+  a.step_size = static_cast<float>(lr / bc1);
+  a.bc2_sqrt = static_cast<float>(std::sqrt(bc2));
+  a.eps = eps;
+  auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+  const int vec = al(w, 15) && al(exp_avg, 15) && al(exp_avg_sq, 15) && al(grad, grad_bf16 ? 7 : 15) &&
+                  (w_bf16 == nullptr || al(w_bf16, 7));
+  if (amax != nullptr) Q2B_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
+  const int64_t want = (n / 4 + 255) / 256;
+  const int blocks = static_cast<int>(want < 1 ? 1 : (want < int64_t(sms) * 8 ? want : int64_t(sms) * 8));
+  auto* wb = static_cast<__nv_bfloat16*>(w_bf16);
+  auto* am = reinterpret_cast<unsigned*>(amax);
+  if (grad_bf16)
+    q2b::adamw_amax_kernel<true><<<blocks, 256, 0, st>>>(w, exp_avg, exp_avg_sq, grad, n, a, wb, am, vec);
+  else
+    q2b::adamw_amax_kernel<false><<<blocks, 256, 0, st>>>(w, exp_avg, exp_avg_sq, grad, n, a, wb, am, vec);
   Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
 }

@@ -165,6 +165,20 @@ int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, co
  * No counterpart in the reference (its GEMM library manages its own). */
 int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
+/* One AdamW step (decoupled weight decay, torch's fused-AdamW operation
+ * order) on n fp32 weights w with fp32 moments exp_avg / exp_avg_sq and an
+ * fp32 (grad_bf16 = 0) or bf16 (grad_bf16 = 1) gradient; step is the 1-based
+ * step count after this update.  In the same pass: *amax = max |w_new| (fp32,
+ * device; written even when it stays 0) when amax is not null, and
+ * w_bf16[i] = bf16(w_new[i]) when w_bf16 is not null.  Any alignment; 16-byte
+ * aligned tensors take the vector path.
+ * Replaces: torch.optim.AdamW(fused=True) (src/models/parametrizations.py:311)
+ * followed by the weight abs-max pass of register_optimizer_hook,
+ * quartet2/python/quartet2/linear.py:259-270. */
+int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad, int grad_bf16, int64_t n,
+                   float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step, void* w_bf16,
+                   float* amax, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,17 @@ def test_ragged_entry_points_reject_bad_arguments():
     assert _lib.load().q2b_gemm_workspace_bytes(1, 100, 128) == 0
 
 
+def test_adamw_rejects_bad_arguments():
+    with pytest.raises(ValueError, match="n must be positive"):
+        _lib.call("q2b_adamw_step", FAKE, FAKE, FAKE, FAKE, 0, 0, 1e-3, 0.9, 0.99, 1e-8, 0.0, 1, None, None, None)
+    with pytest.raises(ValueError, match="step must be >= 1"):
+        _lib.call("q2b_adamw_step", FAKE, FAKE, FAKE, FAKE, 0, 8, 1e-3, 0.9, 0.99, 1e-8, 0.0, 0, None, None, None)
+    with pytest.raises(ValueError, match="betas"):
+        _lib.call("q2b_adamw_step", FAKE, FAKE, FAKE, FAKE, 0, 8, 1e-3, 1.0, 0.99, 1e-8, 0.0, 1, None, None, None)
+    with pytest.raises(ValueError, match="is null"):
+        _lib.call("q2b_adamw_step", None, FAKE, FAKE, FAKE, 0, 8, 1e-3, 0.9, 0.99, 1e-8, 0.0, 1, None, None, None)
+
+
 def test_last_error_is_thread_local_text():
     with pytest.raises(ValueError):
         _lib.call("q2b_gemm_nvfp4", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100, 128, 128, None)
