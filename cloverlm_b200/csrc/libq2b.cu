@@ -244,6 +244,26 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
   return Q2B_OK;
 }
 
+int q2b_relu2_abs_max(void* y, float* amax, const void* a, int64_t n, void* stream) {
+  Q2B_REQUIRE_PTR(y);
+  Q2B_REQUIRE_PTR(a);
+  Q2B_REQUIRE_NONNULL(amax);
+  if (n <= 0) return fail(Q2B_ERR_INVALID, "relu2_abs_max: n must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Q2B_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
+  const int64_t nvec = n / 8;
+  const int64_t want = (nvec + 255) / 256;
+  const int blocks = static_cast<int>(want < 1 ? 1 : (want < int64_t(sms) * 8 ? want : int64_t(sms) * 8));
+  q2b::relu2_abs_max_kernel<<<blocks, 256, 0, st>>>(static_cast<uint4*>(y), reinterpret_cast<unsigned*>(amax),
+                                                    static_cast<const uint4*>(a), nvec,
+                                                    static_cast<uint16_t*>(y) + nvec * 8,
+                                                    static_cast<const uint16_t*>(a) + nvec * 8, n - nvec * 8);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
 static int quant_fwd_impl(void* codes, void* sf, float* ts, const void* x, const float* amax, float scale_override,
                           int64_t rows, int64_t cols, int mode, void* stream, bool ragged) {
   if (mode != Q2B_MODE_RNE && mode != Q2B_MODE_FOUR_SIX)

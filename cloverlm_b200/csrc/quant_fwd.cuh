@@ -285,4 +285,45 @@ __global__ void __launch_bounds__(256) abs_max_kernel(unsigned* __restrict__ out
   }
 }
 
+// y = relu(a)^2 (bf16, from the fp32 square of the bf16 input) and
+// *amax = max |y| in one pass: the MLP activation feeding a Quartet layer
+// together with the abs-max that layer's quantizer needs.  *amax must be zero
+// on entry.  a and y 16-byte aligned; the tail (n % 8) runs in block 0.
+__global__ void __launch_bounds__(256) relu2_abs_max_kernel(uint4* __restrict__ y, unsigned* __restrict__ amax,
+                                                            const uint4* __restrict__ a, int64_t nvec,
+                                                            uint16_t* __restrict__ y_tail,
+                                                            const uint16_t* __restrict__ a_tail, int64_t ntail) {
+  float m = 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const uint4 v = __ldcs(a + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float lo = fmaxf(bf16lo(w[k]), 0.f), hi = fmaxf(bf16hi(w[k]), 0.f);
+      o[k] = pack_bf16x2(lo * lo, hi * hi);
+      m = fmaxf(m, fmaxf(bf16lo(o[k]), bf16hi(o[k])));
+    }
+    y[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t t = threadIdx.x; t < ntail; t += blockDim.x) {
+      const float r = fmaxf(__uint_as_float(static_cast<uint32_t>(a_tail[t]) << 16), 0.f);
+      const uint32_t b = pack_bf16x2(r * r, 0.f) & 0xFFFFu;
+      y_tail[t] = static_cast<uint16_t>(b);
+      m = fmaxf(m, __uint_as_float(b << 16));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (blockDim.x >> 5); ++k) m = fmaxf(m, red[k]);
+    atomicMax(amax, __float_as_uint(m));
+  }
+}
+
 }  // namespace q2b

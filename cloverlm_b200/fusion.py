@@ -1,0 +1,113 @@
+"""Fusions across the ops around the Quartet-II linear.
+
+``shared_input_forward(x, layers)`` -- several Quartet_II_linear layers that
+read the same activation (the attention projections lq, lk, lv of
+src/models/transformer.py:316-322,341-344 all take X).  The reference runs
+three independent Quartet_II_fn calls, each computing abs-max(X) and
+quantizing X; here X is quantized once and the three forward GEMMs share its
+NVFP4 copy.  Forward outputs are bit-identical to separate calls.  Backward
+runs each layer's own backward (quartet_backward, with its own randomized
+Hadamard draw) and sums the input gradients; only the order of the random
+draws differs from separate calls.
+
+``relu2_abs_max(a)`` -- the MLP's ReLU² activation (src/models/mlp.py:34-38,
+the `act` of MLP2L.l1, mlp.py:96-99,113-118) computed together with the
+abs-max of its bf16 output, so the next Quartet layer gets ``input_abs_max``
+and skips its own pass over the activation.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .linear import Quartet_II_linear, _fp4_mm, quartet_backward
+from .quant import NVFP4QuantMode, abs_max, quant_fp4
+
+
+class _SharedInputQuartet(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, mode, input_amax, n, *args):
+        weights, weight_amaxes, hads, scratches = args[:n], args[n:2 * n], args[2 * n:3 * n], args[3 * n:4 * n]
+        if torch.is_autocast_enabled("cuda"):
+            x = x.to(torch.bfloat16)
+        elif x.dtype != torch.bfloat16:
+            raise TypeError("Input must be bfloat16. Either cast input to bfloat16 or enable autocast`")
+        flat = x.reshape(-1, x.shape[-1]).contiguous()
+        if input_amax is None:
+            input_amax = abs_max(flat)
+        xq = quant_fp4(flat, amax=input_amax, scale_override=1.0, mode=mode)
+        outs, saved = [], [xq.fp4, xq.micro_scales, xq.tensor_scale]
+        for w, wa in zip(weights, weight_amaxes):
+            if torch.is_autocast_enabled("cuda"):
+                w = w.to(torch.bfloat16)
+            elif w.dtype != torch.bfloat16:
+                raise TypeError("Weight must be bfloat16. Either set `dtype=torch.bfloat16` or enable autocast`")
+            w = w.contiguous()
+            wq = quant_fp4(w, amax=abs_max(w) if wa is None else wa, scale_override=1.0, mode=mode)
+            y = _fp4_mm(xq.fp4, wq.fp4, xq.micro_scales, wq.micro_scales, alpha=xq.tensor_scale * wq.tensor_scale)
+            outs.append(y.reshape(*x.shape[:-1], w.shape[0]))
+            saved += [wq.fp4, wq.micro_scales, wq.tensor_scale]
+        ctx.save_for_backward(*saved)
+        ctx.hads, ctx.scratches, ctx.n, ctx.x_shape = hads, scratches, n, x.shape
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        saved = ctx.saved_tensors
+        xfp4, xs, xm = saved[:3]
+        dx, dws = None, []
+        for i, g in enumerate(grads):
+            if g is None:
+                dws.append(None)
+                continue
+            wfp4, ws, wm = saved[3 + 3 * i:6 + 3 * i]
+            if torch.is_autocast_enabled("cuda"):
+                g = g.to(torch.bfloat16)
+            gi, gw = quartet_backward(g.reshape(-1, g.shape[-1]).contiguous(), xfp4, xs, xm, wfp4, ws, wm,
+                                      ctx.hads[i], ctx.scratches[i])
+            dx = gi if dx is None else dx + gi
+            dws.append(gw)
+        dx = None if dx is None else dx.reshape(ctx.x_shape)
+        return (dx, None, None, None, *dws, *([None] * (3 * ctx.n)))
+
+
+def shared_input_forward(x: torch.Tensor, layers, input_abs_max: torch.Tensor | None = None):
+    """Outputs of ``layers`` (Quartet_II_linear, same in_features and mode) on one input x,
+    quantizing x once."""
+    layers = list(layers)
+    if not layers or not all(isinstance(m, Quartet_II_linear) for m in layers):
+        raise TypeError("shared_input_forward takes Quartet_II_linear layers")
+    if len({m.in_features for m in layers}) != 1 or len({m.mode for m in layers}) != 1:
+        raise ValueError("layers must share in_features and mode")
+    n = len(layers)
+    args = ([m.weight[...] for m in layers] + [m.weight_abs_max for m in layers] + [m.had for m in layers]
+            + [m.scratch_amax for m in layers])
+    return _SharedInputQuartet.apply(x, layers[0].mode, input_abs_max, n, *args)
+
+
+# ----------------------------------------------------------------- ReLU^2 + abs-max
+
+class _Relu2AbsMax(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a):
+        a = a.contiguous()
+        y = torch.empty_like(a, dtype=torch.bfloat16)
+        amax = torch.empty((), dtype=torch.float32, device=a.device)
+        with torch.cuda.device(a.device):
+            _lib.call("q2b_relu2_abs_max", _lib.ptr(y), _lib.ptr(amax), _lib.ptr(a), a.numel(), _lib.stream_of(a))
+        ctx.save_for_backward(a)
+        ctx.mark_non_differentiable(amax)
+        return y, amax
+
+    @staticmethod
+    def backward(ctx, gy, gamax):
+        (a,) = ctx.saved_tensors
+        # d relu(a)^2 / da = 2 relu(a)
+        return (gy.float() * (2.0 * torch.relu(a.float()))).to(a.dtype)
+
+
+def relu2_abs_max(a: torch.Tensor):
+    """(relu(a)^2 in bf16, max |relu(a)^2| as an fp32 0-d tensor) for bf16 a, one pass."""
+    if a.dtype != torch.bfloat16 or not a.is_cuda:
+        raise TypeError("relu2_abs_max takes a bf16 CUDA tensor")
+    return _Relu2AbsMax.apply(a)

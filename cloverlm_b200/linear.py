@@ -140,32 +140,36 @@ class Quartet_II_fn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output):
         xfp4, xs, xm, wfp4, ws, wm = ctx.saved_tensors
-        backward_scale_override = (17 / 16) * 0.93
         if torch.is_autocast_enabled("cuda"):
             grad_output = grad_output.to(torch.bfloat16)
-        had = rerotate_hadamard(ctx.had)
         flat_grad_output = grad_output.reshape(-1, grad_output.shape[-1]).contiguous()
-
-        if ctx.disable_backward_quant:
-            xr = _dq_fp4(xfp4, xs, xm)
-            wr = _dq_fp4(wfp4, ws, wm)
-            grad_input = flat_grad_output @ wr
-            grad_weight = flat_grad_output.T @ xr
-            return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
-
-        h16 = had[:16, :].contiguous()
-        # E and E^T from one pass over the output gradient
-        e_q, et_q = rht128_quant_eden_dual(h=h16, x=flat_grad_output, scale_override=backward_scale_override,
-                                           scratch_amax=ctx.scratch_amax)
-        wt_q = rht128_requant(x=wfp4, x_group_scales=ws, x_tensor_scale=wm, h=h16,
-                              scale_override=backward_scale_override, scratch_amax=ctx.scratch_amax)
-        grad_input = _fp4_mm(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
-                             alpha=e_q.tensor_scale * wt_q.tensor_scale)
-        xt_q = rht128_requant(x=xfp4, x_group_scales=xs, x_tensor_scale=xm, h=h16,
-                              scale_override=backward_scale_override, scratch_amax=ctx.scratch_amax)
-        grad_weight = _fp4_mm(et_q.fp4, xt_q.fp4, et_q.micro_scales, xt_q.micro_scales,
-                              alpha=et_q.tensor_scale * xt_q.tensor_scale)
+        grad_input, grad_weight = quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, ctx.had,
+                                                   ctx.scratch_amax, ctx.disable_backward_quant)
         return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
+
+
+def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_amax, disable_backward_quant=False):
+    """dX and dW of one Quartet-II linear from the saved NVFP4 operands (linear.py:200-233):
+    rerotate H, EDEN of E and E^T (one pass), requantize W^T and X^T, two NVFP4 GEMMs."""
+    backward_scale_override = (17 / 16) * 0.93
+    had = rerotate_hadamard(had)
+    if disable_backward_quant:
+        xr = _dq_fp4(xfp4, xs, xm)
+        wr = _dq_fp4(wfp4, ws, wm)
+        return flat_grad_output @ wr, flat_grad_output.T @ xr
+    h16 = had[:16, :].contiguous()
+    # E and E^T from one pass over the output gradient
+    e_q, et_q = rht128_quant_eden_dual(h=h16, x=flat_grad_output, scale_override=backward_scale_override,
+                                       scratch_amax=scratch_amax)
+    wt_q = rht128_requant(x=wfp4, x_group_scales=ws, x_tensor_scale=wm, h=h16,
+                          scale_override=backward_scale_override, scratch_amax=scratch_amax)
+    grad_input = _fp4_mm(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
+                         alpha=e_q.tensor_scale * wt_q.tensor_scale)
+    xt_q = rht128_requant(x=xfp4, x_group_scales=xs, x_tensor_scale=xm, h=h16,
+                          scale_override=backward_scale_override, scratch_amax=scratch_amax)
+    grad_weight = _fp4_mm(et_q.fp4, xt_q.fp4, et_q.micro_scales, xt_q.micro_scales,
+                          alpha=et_q.tensor_scale * xt_q.tensor_scale)
+    return grad_input, grad_weight
 
 
 class Quartet_II_linear(torch.nn.Linear):

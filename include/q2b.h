@@ -52,6 +52,12 @@ int q2b_device_status(unsigned* code);
  * Replaces: abs_max (torch.compile reduction), quartet2/python/quartet2/linear.py:146-148. */
 int q2b_abs_max(float* out, const void* x, int64_t n, void* stream);
 
+/* y = relu(a)^2 for n bf16 values and out[0] = max |y| (fp32) in one pass.
+ * a and y 16-byte aligned.
+ * Replaces: the MLP activation ReLU2 (src/models/mlp.py:34-38) and the
+ * abs-max pass of the next Quartet layer's forward (linear.py:146-148,179-183). */
+int q2b_relu2_abs_max(void* y, float* amax, const void* a, int64_t n, void* stream);
+
 /* Forward RTN quantization of bf16 x [rows, cols] to NVFP4 with tensor scale
  * from *amax; mode Q2B_MODE_RNE or Q2B_MODE_FOUR_SIX.
  * Replaces: rtn_fp4 / four_six_fp4, quartet2/csrc/round_four_six.cu:125-153
