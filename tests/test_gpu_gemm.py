@@ -69,6 +69,13 @@ def test_gemm_blocky_scales(M, N, K):
     _check(M, N, K, seed=7, blocky=True)
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 3584, 3584), (2048, 2560, 1408), (2048, 2560, 8192), (2560, 2048, 640)])
+def test_gemm_pair_kernel_shapes(M, N, K):
+    """Shapes whose 256x256 tiles fill the SM pairs take the cta_group::2 kernel (ragged K tails included)."""
+    rel = _check(M, N, K, seed=M + K)
+    assert rel < 5e-3
+
+
 def test_gemm_large_k_wgrad_shape():
     # wgrad-like: long contraction (tokens), small output
     _check(512, 512, 16384, seed=3)
