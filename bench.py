@@ -375,12 +375,80 @@ def run_ours(args) -> None:
     }
     if world == 1 and not args.no_small_m:
         line["small_m"] = small_m_report(dev)
+    if world == 1 and not args.no_quant_sweep:
+        line["quantizer_sweep"] = quant_sweep_report(dev)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_entry(cpu_step_tokens())
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+SWEEP_M = [1024, 16384, 65536]
+SWEEP_K = [3584, 14336]
+
+
+def quant_sweep_report(dev, reps: int = 5) -> dict:
+    """quantizers on bf16 [M, K] ~ Student-t(df=3)/sqrt(3), seed 1, through the public
+    API.  Each call is timed alone with CUDA events after a 256 MB write that evicts L2, so no input
+    is served from L2.  Algorithmic bytes per element: abs-max 2; RTN (RNE, four-over-six) 2 + 0.5625;
+    EDEN with the randomized Hadamard rotation 2 + 0.5625 + 0.25 (bf16 scale scratch written and read
+    by the stochastic-rounding pass) per orientation, the dual-orientation call reading x once."""
+    import torch
+
+    from cloverlm_b200.linear import get_hadamard_matrix
+    from cloverlm_b200.quant import NVFP4QuantMode, abs_max, quant_fp4, rht128_quant_eden, rht128_quant_eden_dual
+
+    peaks = load_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    h = get_hadamard_matrix(128, torch.bfloat16, dev)[:16].contiguous()
+    seed = torch.tensor(1)
+
+    def timed(fn):
+        ts = []
+        for _ in range(reps + 1):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts[1:])
+
+    out = {"unit": "GB/s", "hbm_peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"],
+           "config": "BASELINE config 2: Student-t(3)/sqrt(3) bf16, seed 1; L2 evicted before every call",
+           "shapes": {}}
+    g = torch.Generator(device=dev).manual_seed(1)
+    for M in SWEEP_M:
+        for K in SWEEP_K:
+            z = torch.randn(M, K, device=dev, generator=g)
+            chi = torch.randn(3, M, K, device=dev, generator=g).pow_(2).sum(0)
+            x = (z / torch.sqrt(chi / 3.0) / 3.0 ** 0.5).to(torch.bfloat16)
+            del z, chi
+            am = abs_max(x)
+            n = M * K
+            rows = {
+                "abs_max": (2.0, lambda: abs_max(x)),
+                "rtn_rne": (2.5625, lambda: quant_fp4(x, scale_override=1.0, amax=am, mode=NVFP4QuantMode.RNE)),
+                "rtn_four_six": (2.5625, lambda: quant_fp4(x, scale_override=1.0, amax=am,
+                                                          mode=NVFP4QuantMode.FOUR_SIX)),
+                "eden_rht_rows": (2.8125, lambda: rht128_quant_eden(h=h, x=x, seed=seed, transpose=False)),
+                "eden_rht_cols": (2.8125, lambda: rht128_quant_eden(h=h, x=x, seed=seed, transpose=True)),
+                "eden_rht_dual": (3.625, lambda: rht128_quant_eden_dual(h=h, x=x, seed=seed, seed_t=seed)),
+            }
+            res = {}
+            for name, (bpe, fn) in rows.items():
+                ms = timed(fn)
+                gbs = n * bpe / (ms * 1e-3) / 1e9
+                res[name] = {"gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "us": round(ms * 1e3, 1)}
+            out["shapes"][f"{M}x{K}"] = res
+            del x
+    del flush
+    torch.cuda.empty_cache()
+    return out
 
 
 SMALL_M = [1, 8, 64, 256, 4096]
@@ -457,6 +525,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=65536)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-small-m", action="store_true", help="skip the inference-linear latency section")
+    ap.add_argument("--no-quant-sweep", action="store_true", help="skip the quantizer sweep section")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -217,11 +217,11 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       const float x_ts = *p.x_ts;
       const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
       constexpr int kItems = 128 * 8 / (32 * Cfg::kProdWarps);  // (row, 16-col group) items per thread
-      // registers hold the next tile's codes and scales while this tile is
-      // converted, so global-load latency overlaps the conversion
-      uint2 q[kItems];
-      uint32_t sb[kItems];
-      auto load_tile = [&](int64_t t) {
+      // registers hold the codes and scales of the next TWO tiles while this
+      // tile is converted, so two tiles of conversion hide each global load
+      uint2 qa[kItems], qb[kItems];
+      uint32_t sa[kItems], sbb[kItems];
+      auto load_tile = [&](int64_t t, uint2 (&q)[kItems], uint32_t (&sb)[kItems]) {
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
@@ -235,17 +235,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           sb[u] = p.x_sf[so];
         }
       };
-      if (static_cast<int64_t>(blockIdx.x) < ntiles) load_tile(blockIdx.x);
-      int it = 0;
-      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      auto convert = [&](int it, const uint2 (&qc)[kItems], const uint32_t (&sc)[kItems]) -> bool {
         const int slot = it % kRhtStages;
         const uint32_t ph = (it / kRhtStages) & 1;
-        uint2 qc[kItems];
-        uint32_t sc[kItems];
-#pragma unroll
-        for (int u = 0; u < kItems; ++u) { qc[u] = q[u]; sc[u] = sb[u]; }
-        if (t + gridDim.x < ntiles) load_tile(t + gridDim.x);
-        if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
+        if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
         uint8_t* dst = tiles + slot * kTileBytes;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
@@ -267,6 +260,29 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&full[slot]);
+        return true;
+      };
+      const int64_t step = gridDim.x;
+      int64_t t = blockIdx.x;
+      if (t < ntiles) load_tile(t, qa, sa);
+      if (t + step < ntiles) load_tile(t + step, qb, sbb);
+      int it = 0;
+      while (t < ntiles) {
+        uint2 qc[kItems];
+        uint32_t sc[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) { qc[u] = qa[u]; sc[u] = sa[u]; }
+        if (t + 2 * step < ntiles) load_tile(t + 2 * step, qa, sa);
+        if (!convert(it, qc, sc)) break;
+        t += step;
+        ++it;
+        if (t >= ntiles) break;
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) { qc[u] = qb[u]; sc[u] = sbb[u]; }
+        if (t + 2 * step < ntiles) load_tile(t + 2 * step, qb, sbb);
+        if (!convert(it, qc, sc)) break;
+        t += step;
+        ++it;
       }
     }
   } else if (warp == Cfg::kMmaWarp) {
@@ -341,9 +357,14 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       uint32_t cw[8], fs[4];
+#ifdef Q2B_RHT_PROBE_NO_EPI
+      for (int g = 0; g < 8; ++g) cw[g] = r[g >> 2][g & 3];
+      for (int g = 0; g < 4; ++g) fs[g] = r[1][g];
+#else
 #pragma unroll
       for (int g = 0; g < 4; ++g)
         run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
+#endif
       __stcs(reinterpret_cast<uint4*>(crow), make_uint4(cw[0], cw[1], cw[2], cw[3]));
       __stcs(reinterpret_cast<uint4*>(crow + 16), make_uint4(cw[4], cw[5], cw[6], cw[7]));
       const int64_t kb = ogrp * 8 + colhalf * 4;  // 4 consecutive 16-blocks: one aligned 8-byte store
