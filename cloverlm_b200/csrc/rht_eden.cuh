@@ -222,6 +222,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       uint2 qa[kItems], qb[kItems];
       uint32_t sa[kItems], sbb[kItems];
       auto load_tile = [&](int64_t t, uint2 (&q)[kItems], uint32_t (&sb)[kItems]) {
+#ifdef Q2B_RHT_PROBE_NO_LOAD
+        if (t >= 0) { for (int u = 0; u < kItems; ++u) { q[u] = make_uint2(pt * 0x01010101u, t); sb[u] = 0x38; } return; }
+#endif
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
@@ -240,6 +243,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         const uint32_t ph = (it / kRhtStages) & 1;
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
         uint8_t* dst = tiles + slot * kTileBytes;
+#ifdef Q2B_RHT_PROBE_NO_CONVERT
+        if (true) { fence_proxy_async_smem(); mbar_arrive(&full[slot]); return true; }
+#endif
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
