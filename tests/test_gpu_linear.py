@@ -144,3 +144,44 @@ def test_mlp_relu2_fusion_feeds_the_next_layer_its_abs_max():
     a = l1(x)
     h, amax = relu2_abs_max(a)
     assert torch.equal(l2(h, input_abs_max=amax), l2(torch.relu(a) ** 2))
+
+
+def test_training_step_captures_in_a_cuda_graph():
+    """Forward + backward of a Quartet layer (quantizers, EDEN, requant, three NVFP4 GEMMs, the
+    randomized Hadamard draw) records into one CUDA graph: no host synchronisation on the path.
+    Replays give the eager forward bit for bit; each replay draws fresh Hadamard signs from torch's
+    graph-safe generator (as eager steps do), so its gradients differ from the last replay's but
+    stay as close to the exact gradients as eager ones."""
+    torch.manual_seed(4)
+    layer = Quartet_II_linear(256, 384, bias=False, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(1, 256, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    dy = torch.randn(1, 256, 384, device="cuda", dtype=torch.bfloat16)
+    layer(x, disable_backward_quant=True).backward(dy)
+    exact = (x.grad.clone(), layer.weight.grad.clone())
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):  # warm-up on the capture stream
+            layer.weight.grad = None
+            x.grad = None
+            layer(x).backward(dy)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    layer.weight.grad = None
+    x.grad = None
+    with torch.cuda.graph(g):
+        y = layer(x)
+        y.backward(dy)
+    outs = []
+    for _ in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        outs.append((y.clone(), x.grad.clone(), layer.weight.grad.clone()))
+    with torch.no_grad():
+        eager = layer(x)
+    assert torch.equal(outs[0][0], eager) and torch.equal(outs[1][0], eager)
+    assert not torch.equal(outs[0][1], outs[1][1])  # a new random rotation per replay
+    for _, gx, gw in outs:
+        for got, ref in ((gx, exact[0]), (gw, exact[1])):
+            _, bits, cos = _quality(got, ref)
+            assert bits > 1.7 and abs(cos - 1.0) < 0.1, (bits, cos)
