@@ -19,7 +19,11 @@ decode-sized M it splits K across the SMs and sums the partial tiles in fp32.
 The codes and scales of the real rows are the ones the padded path produces
 (zero padding rows change neither the abs-max nor any group); the output
 equals the padded path's up to fp32 summation order when K is split.
-As in the reference, the bias is added to the bf16 output.
+As in the reference, the bias is added to the bf16 output.  The quantizer
+and the GEMM are torch custom ops (``quartet2::quant_rows``,
+``quartet2::quant_rows_amax``, ``quartet2::fp4_mm_rows``) with fake
+implementations, like the reference's ``quartet2::four_six`` and
+``quartet2::fp4_mm``, so ``torch.compile(fullgraph=True)`` traces ``apply``.
 """
 from __future__ import annotations
 
@@ -85,35 +89,82 @@ def quant_rows(x: torch.Tensor, amax: torch.Tensor | None = None):
     in the blocked layout with zero rows past M, tensor scale fp32 [])."""
     assert x.dtype == torch.bfloat16 and x.is_cuda and x.dim() == 2
     x = x.contiguous()
+    if amax is None:
+        return _quant_rows_op(x)
+    return _quant_rows_amax_op(x, amax)
+
+
+def _quant_rows_out(x):
     m, k = x.shape
     m_pad = (m + 127) // 128 * 128
     codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
     ts = torch.empty((), dtype=torch.float32, device=x.device)
+    return m, k, m_pad, codes, ts
+
+
+@torch.library.custom_op("quartet2::quant_rows", mutates_args=())
+def _quant_rows_op(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Abs-max + four-over-six quantization of x [M, K], any M (torch op so torch.compile traces it)."""
+    m, k, m_pad, codes, ts = _quant_rows_out(x)
     with torch.cuda.device(x.device):
-        if amax is None and m * k // 16 <= FUSED_MAX_GROUPS:
+        if m * k // 16 <= FUSED_MAX_GROUPS:
             scales = torch.empty((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
             _lib.call("q2b_quant_rows_fused", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x), 1.0,
                       m, k, _lib.MODE_FOUR_SIX, _lib.stream_of(x))
             return codes, scales, ts
-        if amax is None:
-            amax = abs_max(x)
+        amax = abs_max(x)
         scales = torch.zeros((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
         _lib.call("q2b_quant_fwd_ragged", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x),
                   _lib.ptr(amax), 1.0, m, k, _lib.MODE_FOUR_SIX, _lib.stream_of(x))
     return codes, scales, ts
 
 
+@torch.library.custom_op("quartet2::quant_rows_amax", mutates_args=())
+def _quant_rows_amax_op(x: torch.Tensor, amax: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Four-over-six quantization of x [M, K], any M, with the tensor abs-max given."""
+    m, k, m_pad, codes, ts = _quant_rows_out(x)
+    scales = torch.zeros((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("q2b_quant_fwd_ragged", _lib.ptr(codes), _lib.ptr(scales), _lib.ptr(ts), _lib.ptr(x),
+                  _lib.ptr(amax), 1.0, m, k, _lib.MODE_FOUR_SIX, _lib.stream_of(x))
+    return codes, scales, ts
+
+
+def _quant_rows_fake_impl(x):
+    m, k = x.shape
+    m_pad = (m + 127) // 128 * 128
+    return (torch.empty((m, k // 2), dtype=torch.uint8, device=x.device),
+            torch.empty((m_pad, k // 16), dtype=torch.float8_e4m3fn, device=x.device),
+            torch.empty((), dtype=torch.float32, device=x.device))
+
+
+@_quant_rows_op.register_fake
+def _quant_rows_fake(x):
+    return _quant_rows_fake_impl(x)
+
+
+@_quant_rows_amax_op.register_fake
+def _quant_rows_amax_fake(x, amax):
+    return _quant_rows_fake_impl(x)
+
+
 def fp4_mm_rows(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_mx: torch.Tensor,
                 alpha: torch.Tensor, alpha_b: torch.Tensor | None = None) -> torch.Tensor:
     """bf16 [M, N] = alpha (* alpha_b) * dq(x) @ dq(w)^T for any M >= 1 (x_mx padded to whole 128-row blocks)."""
-    m, packed_k = x_fp4.shape
-    k = packed_k * 2
-    n = w_fp4.shape[0]
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=x_fp4.device)
     if alpha.dtype != torch.float32:
         alpha = alpha.float()
     if alpha_b is not None and alpha_b.dtype != torch.float32:
         alpha_b = alpha_b.float()
+    return _fp4_mm_rows_op(x_fp4, w_fp4, x_mx, w_mx, alpha, alpha_b)
+
+
+@torch.library.custom_op("quartet2::fp4_mm_rows", mutates_args=())
+def _fp4_mm_rows_op(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_mx: torch.Tensor,
+                    alpha: torch.Tensor, alpha_b: torch.Tensor | None) -> torch.Tensor:
+    m, packed_k = x_fp4.shape
+    k = packed_k * 2
+    n = w_fp4.shape[0]
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x_fp4.device)
     with torch.cuda.device(x_fp4.device):
         lib = _lib.load()
         nbytes = int(lib.q2b_gemm_workspace_bytes(m, n, k))
@@ -123,6 +174,11 @@ def fp4_mm_rows(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_
                   _lib.ptr(w_mx), _lib.ptr(alpha), _lib.ptr(alpha_b), m, n, k, _lib.ptr(ws),
                   nbytes if ws is not None else 0, stream)
     return out
+
+
+@_fp4_mm_rows_op.register_fake
+def _fp4_mm_rows_fake(x_fp4, w_fp4, x_mx, w_mx, alpha, alpha_b):
+    return torch.empty((x_fp4.shape[0], w_fp4.shape[0]), dtype=torch.bfloat16, device=x_fp4.device)
 
 
 def apply(prepared: PreparedWeight, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:

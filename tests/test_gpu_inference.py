@@ -150,3 +150,14 @@ def test_gemm_rows_exact_small_integers():
         B = torch.from_numpy(oracle.dequant(cb.numpy(), sb.numpy(), 1.0)).double()
         ref = (A @ B.T).to(torch.bfloat16)
         assert torch.equal(out.cpu(), ref), m
+
+
+def test_apply_compiles_fullgraph():
+    """The ops of apply are torch custom ops (as the reference's quantizers and _fp4_mm are), so
+    torch.compile traces the inference linear without graph breaks (vLLM compiles its models)."""
+    x, w = _inputs(5, 512, 384, seed=21)
+    p = prepare_weight(w)
+    compiled = torch.compile(lambda t: apply(p, t), fullgraph=True)
+    a, b = compiled(x), apply(p, x)
+    assert a.shape == b.shape
+    assert ((a.float() - b.float()).norm() / b.float().norm()).item() < 4e-3
