@@ -68,7 +68,7 @@ struct RhtCfg {
   static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 8;
   static constexpr int kMmaWarp = kProdWarps;
   static constexpr int kEpiWarp0 = kProdWarps + 1;
-  // two warps per TMEM lane quarter and output orientation, 64 columns each
+  // per output orientation two groups of 4 warps (one per TMEM lane quarter) take alternate tiles
   static constexpr int kEpiWarps = 8 * kNumOut;
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
   static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], Cfg::kEpiWarps);
+      mbar_init(&tempty[b], Cfg::kEpiWarps / 2);  // one group of epilogue warps per buffer
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -336,46 +336,56 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
     const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int orient = (kOut == kOutBoth) ? (e >> 3) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
-    const int colhalf = (e >> 2) & 1;      // which 64 of the group's 128 outputs
-    const uint32_t col_base = ((kOut == kOutBoth && orient == 1) ? 128 : 0) + colhalf * 64;
+    // Two groups of epilogue warps take alternate tiles (group g owns TMEM
+    // buffer g), each warp draining its 32 rows x 128 columns in two 64-column
+    // chunks: while one group waits for its TMEM loads the other computes.
+    const int grp = (e >> 2) & 1;
+    const uint32_t col_base = (kOut == kOutBoth && orient == 1) ? 128 : 0;
     uint8_t* codes = orient == 0 ? p.codes_r : p.codes_c;
     uint16_t* scratch = orient == 0 ? p.scratch_r : p.scratch_c;
     unsigned* maxp = orient == 0 ? p.max_r : p.max_c;
     const int64_t out_cols = orient == 0 ? p.N : p.M;  // length of an output row
     const int64_t n_kblk = out_cols >> 4, n_kt = n_kblk >> 2;
     float run_max = 0.f;
-    int it = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const int buf = it & 1;
+    for (int it = grp;; it += 2) {
+      const int64_t t = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
+      if (t >= ntiles) break;
+      const int buf = grp;
       const uint32_t bph = (it >> 1) & 1;
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
       const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
       const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
-      uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + colhalf * 32;
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
-      uint32_t r[2][32];
-      tmem_ld_32x32b_x32(taddr, r[0]);
-      tmem_ld_32x32b_x32(taddr + 32, r[1]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
-      uint32_t cw[8], fs[4];
+      const uint32_t taddr0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
+#pragma unroll
+      for (int colhalf = 0; colhalf < 2; ++colhalf) {
+        uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + colhalf * 32;
+        const uint32_t taddr = taddr0 + colhalf * 64;
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(taddr, r[0]);
+        tmem_ld_32x32b_x32(taddr + 32, r[1]);
+        tmem_ld_wait();
+        if (colhalf == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+        uint32_t cw[8], fs[4];
 #ifdef Q2B_RHT_PROBE_NO_EPI
-      for (int g = 0; g < 8; ++g) cw[g] = r[g >> 2][g & 3];
-      for (int g = 0; g < 4; ++g) fs[g] = r[1][g];
+        for (int g = 0; g < 8; ++g) cw[g] = r[g >> 2][g & 3];
+        for (int g = 0; g < 4; ++g) fs[g] = r[1][g];
 #else
 #pragma unroll
-      for (int g = 0; g < 4; ++g)
-        run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
+        for (int g = 0; g < 4; ++g)
+          run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
 #endif
-      __stcs(reinterpret_cast<uint4*>(crow), make_uint4(cw[0], cw[1], cw[2], cw[3]));
-      __stcs(reinterpret_cast<uint4*>(crow + 16), make_uint4(cw[4], cw[5], cw[6], cw[7]));
-      const int64_t kb = ogrp * 8 + colhalf * 4;  // 4 consecutive 16-blocks: one aligned 8-byte store
-      const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2);
-      *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
+        __stcs(reinterpret_cast<uint4*>(crow), make_uint4(cw[0], cw[1], cw[2], cw[3]));
+        __stcs(reinterpret_cast<uint4*>(crow + 16), make_uint4(cw[4], cw[5], cw[6], cw[7]));
+        const int64_t kb = ogrp * 8 + colhalf * 4;
+        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2);
+        *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) run_max = fmaxf(run_max, __shfl_xor_sync(0xffffffffu, run_max, o));
