@@ -209,36 +209,39 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           mbar_wait(&full[k % kRhtStages], (k / kRhtStages) & 1, kTimeoutProducer);
       }
     } else {
-      // NVFP4 input: each producer thread dequantizes whole 16-element groups
-      // of the tile (8 code bytes + 1 scale byte -> 32 bytes of bf16); eight
-      // consecutive lanes cover one row's 64-byte code segment, so a warp's
-      // loads are contiguous 64-byte runs.
+      // NVFP4 input: each producer thread dequantizes pairs of 16-element
+      // groups of the tile (16 code bytes + 2 scale bytes -> 64 bytes of bf16);
+      // four consecutive lanes cover one row's 64-byte code segment, so a
+      // warp's 16-byte loads are contiguous 64-byte runs of 8 rows.
       const int pt = threadIdx.x;  // 0 .. 32*kProdWarps-1
       const float x_ts = *p.x_ts;
       const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
-      constexpr int kItems = 128 * 8 / (32 * Cfg::kProdWarps);  // (row, 16-col group) items per thread
+      constexpr int kItems = 128 * 4 / (32 * Cfg::kProdWarps);  // (row, group pair) items per thread
       // registers hold the codes and scales of the next TWO tiles while this
       // tile is converted, so two tiles of conversion hide each global load
-      uint2 qa[kItems], qb[kItems];
+      uint4 qa[kItems], qb[kItems];
       uint32_t sa[kItems], sbb[kItems];
-      auto load_tile = [&](int64_t t, uint2 (&q)[kItems], uint32_t (&sb)[kItems]) {
+      auto load_tile = [&](int64_t t, uint4 (&q)[kItems], uint32_t (&sb)[kItems]) {
 #ifdef Q2B_RHT_PROBE_NO_LOAD
-        if (t >= 0) { for (int u = 0; u < kItems; ++u) { q[u] = make_uint2(pt * 0x01010101u, t); sb[u] = 0x38; } return; }
+        if (t >= 0) {
+          for (int u = 0; u < kItems; ++u) { q[u] = make_uint4(pt * 0x01010101u, t, pt, t); sb[u] = 0x3838; }
+          return;
+        }
 #endif
         const int64_t tm = t / tiles_n, tn = t % tiles_n;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
-          const int r = item >> 3, g = item & 7;  // row, 16-col group of the tile
+          const int r = item >> 2, gp = item & 3;  // row, pair of 16-col groups of the tile
           const int64_t row = tm * 128 + r;
-          q[u] = __ldcs(reinterpret_cast<const uint2*>(p.x_codes + row * (p.N >> 1) + tn * 64 + g * 8));
-          const int64_t kb = tn * 8 + g;
+          q[u] = __ldcs(reinterpret_cast<const uint4*>(p.x_codes + row * (p.N >> 1) + tn * 64 + gp * 16));
+          const int64_t kb = tn * 8 + 2 * gp;  // even: the pair's two scale bytes are adjacent
           const int64_t so = (((row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2) |
                              (kb & 3);
-          sb[u] = p.x_sf[so];
+          sb[u] = *reinterpret_cast<const uint16_t*>(p.x_sf + so);
         }
       };
-      auto convert = [&](int it, const uint2 (&qc)[kItems], const uint32_t (&sc)[kItems]) -> bool {
+      auto convert = [&](int it, const uint4 (&qc)[kItems], const uint32_t (&sc)[kItems]) -> bool {
         const int slot = it % kRhtStages;
         const uint32_t ph = (it / kRhtStages) & 1;
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
@@ -249,19 +252,23 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
-          const int r = item >> 3, g = item & 7;
-          const float gs = e4m3_to_f32(sc[u]) * x_ts;
+          const int r = item >> 2, gp = item & 3;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {  // 8 elements -> one 16-byte chunk
-            const uint32_t w = half ? qc[u].y : qc[u].x;
-            uint32_t o[4];
+          for (int k = 0; k < 2; ++k) {  // the pair's two groups
+            const int g = 2 * gp + k;
+            const float gs = e4m3_to_f32((sc[u] >> (8 * k)) & 0xFFu) * x_ts;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const float2 dq = f16x2_to_f32x2(e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu));
-              const float2 v = fmul2(dq, make_float2(gs, gs));
-              o[b] = pack_bf16x2(v.x, v.y);
+            for (int half = 0; half < 2; ++half) {  // 8 elements -> one 16-byte chunk
+              const uint32_t w = k == 0 ? (half ? qc[u].y : qc[u].x) : (half ? qc[u].w : qc[u].z);
+              uint32_t o[4];
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const float2 dq = f16x2_to_f32x2(e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu));
+                const float2 v = fmul2(dq, make_float2(gs, gs));
+                o[b] = pack_bf16x2(v.x, v.y);
+              }
+              *reinterpret_cast<uint4*>(dst + tile_off(r, 16 * g + 8 * half)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
-            *reinterpret_cast<uint4*>(dst + tile_off(r, 16 * g + 8 * half)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_proxy_async_smem();
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       if (t + step < ntiles) load_tile(t + step, qb, sbb);
       int it = 0;
       while (t < ntiles) {
-        uint2 qc[kItems];
+        uint4 qc[kItems];
         uint32_t sc[kItems];
 #pragma unroll
         for (int u = 0; u < kItems; ++u) { qc[u] = qa[u]; sc[u] = sa[u]; }
