@@ -1,0 +1,126 @@
+"""Same-box timing of the reference's own GPU path against ours on the four 4B linears
+(SURVEY.md-style "reference GPU baseline", BASELINE config 3 at 16384 tokens to keep the
+test short): the reference's quantizer kernels built from its sources (oracle/_ref/libq2ref.so,
+see oracle/Makefile) plus FlashInfer's cuDNN NVFP4 GEMM, composed as Quartet_II_fn does
+(quartet2/python/quartet2/linear.py:155-233), against cloverlm_b200's kernels.  Prints the
+per-op table (run with -s); asserts only that both paths ran and ours is not slower than 1.5x."""
+import ctypes
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REF_SO = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "libq2ref.so")
+SO = (17 / 16) * 0.93
+SHAPES = [("qkv", 3584, 10752), ("attn_out", 3584, 3584), ("mlp_up", 3584, 14336), ("mlp_down", 14336, 3584)]
+
+
+def _timed(fn, reps=5):
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def test_reference_gpu_path_vs_ours():
+    if not os.path.exists(REF_SO):
+        pytest.skip("reference kernels not built (oracle/_ref/libq2ref.so)")
+    mm_fp4 = pytest.importorskip("flashinfer").mm_fp4
+    from cloverlm_b200.linear import _fp4_mm, get_hadamard_matrix
+    from cloverlm_b200.quant import NVFP4QuantMode, abs_max, quant_fp4, rht128_quant_eden_dual, rht128_requant
+
+    L = ctypes.CDLL(REF_SO)
+    P, F, L64, I = ctypes.c_void_p, ctypes.c_float, ctypes.c_long, ctypes.c_int
+    L.qref_quant_fwd.argtypes = [P, P, P, P, P, F, L64, L64, I]
+    L.qref_rht128_eden.argtypes = [P, P, P, P, P, P, P, L64, F, F, I, I, I, I]
+    L.qref_rht128_requant.argtypes = [P, P, P, P, P, P, P, P, P, L64, F, F, I, I]
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    e8 = lambda n: torch.empty(n, dtype=torch.uint8, device="cuda")
+
+    def ref_quant(x, amax):
+        r, c = x.shape
+        y, s, t = e8(r * c // 2), e8(r * c // 16), torch.empty((), device="cuda")
+        assert L.qref_quant_fwd(p(y), p(s), p(t), p(x), p(amax), 1.0, r, c, 1) == 0
+        return y.view(r, c // 2), s, t
+
+    def ref_eden(x, h, tr):
+        M, N = x.shape
+        rows, cols = (N, M) if tr else (M, N)
+        y, s, t = e8(rows * cols // 2), e8(rows * cols // 16), torch.empty((), device="cuda")
+        sc = torch.empty(rows * cols // 16, dtype=torch.bfloat16, device="cuda")
+        mx = torch.zeros((), dtype=torch.int32, device="cuda")
+        assert L.qref_rht128_eden(p(y), p(s), p(t), p(sc), p(mx), p(h), p(x), 42, 6.0 / SO, 256.0, M, N, int(tr), 0) == 0
+        return y.view(rows, cols // 2), s, t
+
+    def ref_requant(q, s, t, h, M, N):
+        y, so, ts = e8(N * M // 2), e8(N * M // 16), torch.empty((), device="cuda")
+        sc = torch.empty(N * M // 16, dtype=torch.bfloat16, device="cuda")
+        mx = torch.zeros((), dtype=torch.int32, device="cuda")
+        assert L.qref_rht128_requant(p(y), p(so), p(ts), p(sc), p(mx), p(h), p(q), p(s), p(t), 7, 6.0 / SO, 256.0,
+                                     M, N) == 0
+        return y.view(N, M // 2), so, ts
+
+    def cudnn(a, b, sa, sb, alpha, M, N, K):
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        return mm_fp4(a, b.T, sa.view(torch.float8_e4m3fn).view(-1, K // 16),
+                      sb.view(torch.float8_e4m3fn).view(-1, K // 16).T, alpha, torch.bfloat16, out, block_size=16,
+                      use_8x4_sf_layout=False, backend="cudnn", use_nvfp4=True)
+
+    h = get_hadamard_matrix(128, torch.bfloat16, "cuda")[:16].contiguous()
+    M = 16384
+    tot = {"ref": 0.0, "ours": 0.0}
+    rows = []
+    for name, K, N in SHAPES:
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        e = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+        xam, wam = x.float().abs().max(), w.float().abs().max()
+        qx, qw = ref_quant(x, xam), ref_quant(w, wam)
+        ee, wt = ref_eden(e, h, False), ref_requant(qw[0], qw[1], qw[2], h, N, K)
+        et, xt = ref_eden(e, h, True), ref_requant(qx[0], qx[1], qx[2], h, M, K)
+        ref = {
+            "abs_max": _timed(lambda: x.abs().max().float()),
+            "quant": _timed(lambda: ref_quant(x, xam)) + _timed(lambda: ref_quant(w, wam)),
+            "eden": _timed(lambda: ref_eden(e, h, False)) + _timed(lambda: ref_eden(e, h, True)),
+            "requant": _timed(lambda: ref_requant(qw[0], qw[1], qw[2], h, N, K))
+                       + _timed(lambda: ref_requant(qx[0], qx[1], qx[2], h, M, K)),
+            "gemm": _timed(lambda: cudnn(qx[0], qw[0], qx[1], qw[1], qx[2] * qw[2], M, N, K))
+                    + _timed(lambda: cudnn(ee[0], wt[0], ee[1], wt[1], ee[2] * wt[2], M, K, N))
+                    + _timed(lambda: cudnn(et[0], xt[0], et[1], xt[1], et[2] * xt[2], N, K, M)),
+        }
+        am = abs_max(x)
+        ox = quant_fp4(x, scale_override=1.0, amax=am, mode=NVFP4QuantMode.FOUR_SIX)
+        ow = quant_fp4(w, scale_override=1.0, amax=wam, mode=NVFP4QuantMode.FOUR_SIX)
+        ours = {
+            "abs_max": _timed(lambda: abs_max(x)),
+            "quant": _timed(lambda: quant_fp4(x, scale_override=1.0, amax=am, mode=NVFP4QuantMode.FOUR_SIX))
+                     + _timed(lambda: quant_fp4(w, scale_override=1.0, amax=wam, mode=NVFP4QuantMode.FOUR_SIX)),
+            "eden": _timed(lambda: rht128_quant_eden_dual(h=h, x=e, seed=torch.tensor(1), seed_t=torch.tensor(2))),
+            "requant": _timed(lambda: rht128_requant(x=ow.fp4, x_group_scales=ow.micro_scales,
+                                                     x_tensor_scale=ow.tensor_scale, h=h, seed=torch.tensor(3)))
+                       + _timed(lambda: rht128_requant(x=ox.fp4, x_group_scales=ox.micro_scales,
+                                                       x_tensor_scale=ox.tensor_scale, h=h, seed=torch.tensor(3))),
+            "gemm": _timed(lambda: _fp4_mm(ox.fp4, ow.fp4, ox.micro_scales, ow.micro_scales, alpha=ox.tensor_scale))
+                    + _timed(lambda: _fp4_mm(ee[0], wt[0], ee[1], wt[1], ee[2] * wt[2]))
+                    + _timed(lambda: _fp4_mm(et[0], xt[0], et[1], xt[1], et[2] * xt[2])),
+        }
+        tot["ref"] += sum(ref.values())
+        tot["ours"] += sum(ours.values())
+        rows.append((name, ref, ours))
+        del x, w, e
+    torch.cuda.empty_cache()
+    for name, ref, ours in rows:
+        print(f"\n{name:9s} " + "  ".join(f"{k} {ref[k]:.3f}/{ours[k]:.3f}" for k in ref) + "  (ms, reference/ours)")
+    flop = 6 * M * sum(K * N for _, K, N in SHAPES)
+    print(f"step ms: reference {tot['ref']:.2f} ({flop / tot['ref'] / 1e9:.0f} TFLOP/s), "
+          f"ours {tot['ours']:.2f} ({flop / tot['ours'] / 1e9:.0f} TFLOP/s)")
+    assert tot["ours"] < 1.5 * tot["ref"]
