@@ -68,11 +68,17 @@ struct RhtCfg {
   static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 8;
   static constexpr int kMmaWarp = kProdWarps;
   static constexpr int kEpiWarp0 = kProdWarps + 1;
-  // per output orientation two groups of 4 warps (one per TMEM lane quarter) take alternate tiles
-  static constexpr int kEpiWarps = 8 * kNumOut;
+  // Groups of 4 epilogue warps (one per TMEM lane quarter) take tiles in turn,
+  // group g draining TMEM buffer g: two groups per orientation for the dual
+  // output (2 buffers x 256 columns), four for one orientation (4 x 128).
+  static constexpr int kEpiGroups = (kNumOut == 2) ? 2 : 4;
+  static constexpr int kEpiWarps = 16;
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
   static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
-  static constexpr uint32_t kTmemCols = 2 * kColsPerBuf;  // 256 or 512
+  static constexpr uint32_t kTmemCols = kEpiGroups * kColsPerBuf;  // 512
+  // columns per TMEM round trip of an epilogue warp: 32 keeps the 800-thread
+  // requant block within 80 registers a thread
+  static constexpr int kChunkCols = (kIn == kInFp4) ? 32 : 64;
   // shared memory: [H 32K][stages x 32K][barriers]
   static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kRhtStages) + 256;
 };
@@ -155,8 +161,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(tiles + kRhtStages * kTileBytes);
   uint64_t* empty = full + kRhtStages;
   uint64_t* tfull = empty + kRhtStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;  // the MMA warp's final commit: no MMA in flight at dealloc
+  uint64_t* tempty = tfull + 4;
+  uint64_t* drain = tempty + 4;  // the MMA warp's final commit: no MMA in flight at dealloc
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,9 +174,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       mbar_init(&full[s], kIn == kInBf16 ? 1 : 32 * Cfg::kProdWarps);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Cfg::kEpiGroups; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], Cfg::kEpiWarps / 2);  // one group of epilogue warps per buffer
+      mbar_init(&tempty[b], 4 * Cfg::kNumOut);  // the group(s) of epilogue warps of this buffer
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -308,8 +314,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
       const int slot = it % kRhtStages;
       const uint32_t ph = (it / kRhtStages) & 1;
-      const int buf = it & 1;
-      const uint32_t bph = (it >> 1) & 1;
+      const int buf = it % Cfg::kEpiGroups;
+      const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
       ok = mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty) && mbar_wait(&full[slot], ph, kTimeoutTmaFull);
       if (!ok) break;
       tc_fence_after();
@@ -343,22 +349,23 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
     const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int orient = (kOut == kOutBoth) ? (e >> 3) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
-    // Two groups of epilogue warps take alternate tiles (group g owns TMEM
-    // buffer g), each warp draining its 32 rows x 128 columns in two 64-column
-    // chunks: while one group waits for its TMEM loads the other computes.
-    const int grp = (e >> 2) & 1;
+    // Groups of epilogue warps take tiles in turn (group g owns TMEM buffer
+    // g), each warp draining its 32 rows x 128 columns in chunks: while one
+    // group waits for its TMEM loads the others compute.
+    const int grp = (e >> 2) % Cfg::kEpiGroups;
     const uint32_t col_base = (kOut == kOutBoth && orient == 1) ? 128 : 0;
     uint8_t* codes = orient == 0 ? p.codes_r : p.codes_c;
     uint16_t* scratch = orient == 0 ? p.scratch_r : p.scratch_c;
     unsigned* maxp = orient == 0 ? p.max_r : p.max_c;
     const int64_t out_cols = orient == 0 ? p.N : p.M;  // length of an output row
     const int64_t n_kblk = out_cols >> 4, n_kt = n_kblk >> 2;
+    constexpr int kChunk = Cfg::kChunkCols, kNChunks = 128 / kChunk, kG = kChunk / 16;
     float run_max = 0.f;
-    for (int it = grp;; it += 2) {
+    for (int it = grp;; it += Cfg::kEpiGroups) {
       const int64_t t = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
       if (t >= ntiles) break;
       const int buf = grp;
-      const uint32_t bph = (it >> 1) & 1;
+      const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
@@ -366,32 +373,37 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
       const uint32_t taddr0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
 #pragma unroll
-      for (int colhalf = 0; colhalf < 2; ++colhalf) {
-        uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + colhalf * 32;
-        const uint32_t taddr = taddr0 + colhalf * 64;
-        uint32_t r[2][32];
-        tmem_ld_32x32b_x32(taddr, r[0]);
-        tmem_ld_32x32b_x32(taddr + 32, r[1]);
+      for (int ch = 0; ch < kNChunks; ++ch) {
+        uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + ch * (kChunk / 2);
+        const uint32_t taddr = taddr0 + ch * kChunk;
+        uint32_t r[kChunk / 32][32];
+#pragma unroll
+        for (int h = 0; h < kChunk / 32; ++h) tmem_ld_32x32b_x32(taddr + 32 * h, r[h]);
         tmem_ld_wait();
-        if (colhalf == 1) {
+        if (ch == kNChunks - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
-        uint32_t cw[8], fs[4];
+        uint32_t cw[2 * kG], fs[kG];
 #ifdef Q2B_RHT_PROBE_NO_EPI
-        for (int g = 0; g < 8; ++g) cw[g] = r[g >> 2][g & 3];
-        for (int g = 0; g < 4; ++g) fs[g] = r[1][g];
+        for (int g = 0; g < 2 * kG; ++g) cw[g] = r[0][g];
+        for (int g = 0; g < kG; ++g) fs[g] = r[0][g + 8];
 #else
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
+        for (int g = 0; g < kG; ++g)
           run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
 #endif
-        __stcs(reinterpret_cast<uint4*>(crow), make_uint4(cw[0], cw[1], cw[2], cw[3]));
-        __stcs(reinterpret_cast<uint4*>(crow + 16), make_uint4(cw[4], cw[5], cw[6], cw[7]));
-        const int64_t kb = ogrp * 8 + colhalf * 4;
-        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2);
-        *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
+#pragma unroll
+        for (int v = 0; v < kG / 2; ++v)
+          __stcs(reinterpret_cast<uint4*>(crow + 16 * v), make_uint4(cw[4 * v], cw[4 * v + 1], cw[4 * v + 2], cw[4 * v + 3]));
+        const int64_t kb = ogrp * 8 + ch * kG;
+        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2) |
+                           (kb & 3);
+        if constexpr (kG == 4)
+          *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
+        else
+          *reinterpret_cast<uint32_t*>(scratch + so) = fs[0] | (fs[1] << 16);
       }
     }
 #pragma unroll
