@@ -25,11 +25,11 @@
 //     (rotation along the contiguous dimension: `rows` output) and as an
 //     MN-major A operand (rotation along the row dimension: transposed `cols`
 //     output), so E and E^T are both produced from ONE read of E.
-//   * fp32 results land in TMEM (double-buffered).  Eight epilogue warps per
-//     output orientation: two per TMEM lane quarter (32 output rows), each
-//     taking 64 of the 128 rotated values; a thread runs EDEN on four whole
-//     16-groups of its row with no shuffles, writing 32 code bytes and four
-//     bf16 scales.
+//   * fp32 results land in TMEM, one buffer per group of four epilogue warps
+//     (one warp per TMEM lane quarter, 32 output rows); the groups take tiles
+//     in turn (two per orientation for the dual output, four for one
+//     orientation).  A thread runs EDEN on whole 16-groups of its row with no
+//     shuffles, writing the code bytes and bf16 scales of each chunk.
 // Scratch scales are written in the blocked 128x4 layout so the scale pass
 // (sr_scales.cuh) is a flat, fully coalesced map.
 #pragma once
