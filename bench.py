@@ -373,6 +373,11 @@ def run_ours(args) -> None:
         "clocks": clocks,
         "lib": _lib.lib_path(),
     }
+    if world == 1:
+        pk = fp4_mma_peak_report(dev)
+        line["roofline"]["fp4_mma_peak_measured"] = pk
+        if achieved:
+            line["roofline"]["frac_of_fp4_mma_peak"] = achieved / pk["tflops"]
     if world == 1 and not args.no_small_m:
         line["small_m"] = small_m_report(dev)
     if world == 1 and not args.no_quant_sweep:
@@ -383,6 +388,30 @@ def run_ours(args) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def fp4_mma_peak_report(dev, iters: int = 4096, reps: int = 3) -> dict:
+    """The tensor pipe's FP4 ceiling on this GPU: q2b_fp4_mma_peak (back-to-back
+    cta_group::2 M256 N256 K64 NVFP4 MMAs on resident shared-memory operands,
+    one SM pair per two SMs), timed with CUDA events; median of `reps`."""
+    import torch
+    from cloverlm_b200 import _lib
+    stream = torch.cuda.current_stream(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    _lib.call("q2b_fp4_mma_peak", 256, stream.cuda_stream)
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _lib.call("q2b_fp4_mma_peak", iters, stream.cuda_stream)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = sorted(times)[len(times) // 2]
+    flop = (sms // 2) * iters * 2.0 * 256 * 256 * 64
+    return {"tflops": flop / (ms / 1e3) / 1e12, "ms": ms, "iters": iters, "sm_pairs": sms // 2,
+            "note": "q2b_fp4_mma_peak: back-to-back cta_group::2 M256 N256 K64 block-scaled MMAs, "
+                    "operands resident in shared memory"}
 
 
 SWEEP_M = [1024, 16384, 65536]

@@ -666,4 +666,77 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   cluster_sync();
 }
 
+
+// ---------------------------------------------------------------------------
+// FP4 tensor-core peak probe (measurement only).  Each SM pair issues `iters`
+// back-to-back cta_group::2 M256 N256 K64 block-scaled MMAs
+// (2*256*256*64 FLOP each) on operands resident in shared memory: pseudo-random
+// E2M1 codes and E4M3 scales in [0.5, 1.875], so the datapath toggles as in a
+// real GEMM.  No loads and no scale copies inside the loop: the rate is the
+// tensor pipe's own ceiling on this part, the denominator the GEMM kernels'
+// roofline fraction is quoted against.
+struct PeakCfg {
+  static constexpr uint32_t kOpBytes = 2 * 128 * 128;  // A and this CTA's half of B, K = 256
+  static constexpr uint32_t kSfBytes = 2048 + 4096;
+  static constexpr uint32_t kSmemBytes = 1024 + kOpBytes + kSfBytes + 64;
+  static constexpr int kThreads = 128;
+};
+
+__global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int iters) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* drain = reinterpret_cast<uint64_t*>(smem + PeakCfg::kOpBytes + PeakCfg::kSfBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t rank = cluster_ctarank();
+  for (uint32_t i = threadIdx.x; i < PeakCfg::kOpBytes / 4; i += blockDim.x) {
+    uint32_t h = (i + 1u) * 0x9E3779B1u ^ (blockIdx.x * 0x85EBCA77u);
+    h ^= h >> 15;
+    reinterpret_cast<uint32_t*>(smem)[i] = h * 0x2C1B3C6Du;
+  }
+  for (uint32_t i = threadIdx.x; i < PeakCfg::kSfBytes; i += blockDim.x)
+    smem[PeakCfg::kOpBytes + i] = static_cast<uint8_t>(0x30u + ((i * 7u) & 0xFu));  // 0.5 .. 1.875
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  cluster_sync();
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  if (rank == 0 && threadIdx.x == 32) {
+    const uint32_t base = smem_u32(smem);
+    const uint64_t sf_d0 = smem_desc(base + PeakCfg::kOpBytes, 0, 128, kLayoutNone);
+    const uint64_t sfb_d0 = sf_d0 + (2048 >> 4);
+    const uint32_t set = tmem + 256;
+    for (int j = 0; j < 4; ++j) {
+      tmem_cp_32x128b_x4_pair(set + 4 * j, sf_d0 + 32 * j);
+      tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + 32 * j);
+      tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
+    }
+    const uint32_t idesc = idesc_nvf4(256, 256);
+    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
+    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
+    for (int i = 0; i < iters; ++i) {
+      const int j = i & 3;
+      umma_nvf4_pair(tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j, i > 0 ? 1u : 0u);
+    }
+    tc_commit_pair_leader(drain);
+    mbar_wait(drain, 0, kTimeoutProducer);
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+  cluster_sync();
+}
+
 }  // namespace q2b

@@ -101,6 +101,7 @@ int device_setup(int* dev_out, int* sms_out) {
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256>, GemmCfg<256>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128>, GemmCfg<128>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(fp4_mma_peak_kernel, PeakCfg::kSmemBytes));
     d.ready = true;
   }
   *dev_out = dev;
@@ -680,6 +681,26 @@ int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, co
   if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
     return fail(Q2B_ERR_INVALID, "fp4_mm_ex: workspace must be 16-byte aligned");
   return gemm_launch(D, A, B, sfa, sfb, alpha, alpha_b, M, N, K, workspace, workspace_bytes, stream);
+}
+
+int q2b_fp4_mma_peak(int iters, void* stream) {
+  if (iters <= 0 || iters > (1 << 24)) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: iters must be in 1 .. 2^24");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2), 1, 1);
+  cfg.blockDim = dim3(q2b::PeakCfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = q2b::PeakCfg::kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters));
+  return Q2B_OK;
 }
 
 }  // extern "C"

@@ -185,6 +185,13 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
                    float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step, void* w_bf16,
                    float* amax, void* stream);
 
+/* Measurement: one SM pair per two SMs issues `iters` back-to-back
+ * cta_group::2 M256 N256 K64 NVFP4 block-scaled MMAs on operands resident in
+ * shared memory (2*256*256*64 FLOP each; total FLOP = (SMs/2) * iters * that).
+ * Time it with events on `stream` for the tensor pipe's FP4 ceiling.
+ * No counterpart in the reference (its FP4 GEMM is a library call). */
+int q2b_fp4_mma_peak(int iters, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

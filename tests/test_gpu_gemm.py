@@ -103,3 +103,21 @@ def test_gemm_rejects_bad_shapes():
     s = torch.zeros(128 * 5, dtype=torch.uint8, device="cuda").view(torch.float8_e4m3fn)
     with pytest.raises(ValueError, match="K must be divisible by 64"):
         _fp4_mm(a, a, s, s, torch.ones((), device="cuda"))
+
+
+@pytest.mark.gpu
+def test_fp4_mma_peak_probe_runs_in_range():
+    """The FP4 tensor-pipe probe completes with no watchdog trip, at a rate
+    between a plausible floor and twice the nominal dense FP4 figure."""
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream(dev)
+    _lib.call("q2b_fp4_mma_peak", 64, stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    _lib.call("q2b_fp4_mma_peak", 1024, stream.cuda_stream)
+    e1.record(stream)
+    e1.synchronize()
+    assert _lib.device_status() == 0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    tflops = (sms // 2) * 1024 * 2.0 * 256 * 256 * 64 / (e0.elapsed_time(e1) / 1e3) / 1e12
+    assert 2000 < tflops < 18000, tflops
