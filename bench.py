@@ -398,12 +398,12 @@ def fp4_mma_peak_report(dev, iters: int = 4096, reps: int = 3) -> dict:
     from cloverlm_b200 import _lib
     stream = torch.cuda.current_stream(dev)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    _lib.call("q2b_fp4_mma_peak", 256, stream.cuda_stream)
+    _lib.call("q2b_fp4_mma_peak", 256, 0, None, stream.cuda_stream)
     times = []
     for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        _lib.call("q2b_fp4_mma_peak", iters, stream.cuda_stream)
+        _lib.call("q2b_fp4_mma_peak", iters, 0, None, stream.cuda_stream)
         e1.record(stream)
         e1.synchronize()
         times.append(e0.elapsed_time(e1))

@@ -432,6 +432,30 @@ __device__ __forceinline__ void umma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc,
       : "memory");
 }
 
+// The same MMA and commit issued only where `issue` is set, without a branch:
+// the whole warp runs the issue loop converged and one lane issues.
+__device__ __forceinline__ void umma_nvf4_pair_if(bool issue, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "setp.ne.b32 q, %7, 0;\n\t"
+      "@q tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_pair_if(bool issue, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\t.reg .pred q;\n\tmov.b16 m, 3;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar)), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
 // Scale-factor copy into both CTAs' TMEM, each from its own shared memory.
 __device__ __forceinline__ void tmem_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");

@@ -683,8 +683,9 @@ int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, co
   return gemm_launch(D, A, B, sfa, sfb, alpha, alpha_b, M, N, K, workspace, workspace_bytes, stream);
 }
 
-int q2b_fp4_mma_peak(int iters, void* stream) {
-  if (iters <= 0 || iters > (1 << 24)) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: iters must be in 1 .. 2^24");
+int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
+  if (iters <= 0 || iters % 4 != 0 || iters > (1 << 24)) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: iters must be a positive multiple of 4 up to 2^24");
+  if (mode < 0 || mode > 13) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: mode must be 0 .. 13");
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaLaunchConfig_t cfg = {};
@@ -699,7 +700,7 @@ int q2b_fp4_mma_peak(int iters, void* stream) {
   cfg.stream = static_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters));
+  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters, mode, cycles));
   return Q2B_OK;
 }
 

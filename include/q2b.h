@@ -188,9 +188,16 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
 /* Measurement: one SM pair per two SMs issues `iters` back-to-back
  * cta_group::2 M256 N256 K64 NVFP4 block-scaled MMAs on operands resident in
  * shared memory (2*256*256*64 FLOP each; total FLOP = (SMs/2) * iters * that).
- * Time it with events on `stream` for the tensor pipe's FP4 ceiling.
+ * Time it with events on `stream` for the tensor pipe's FP4 ceiling (mode 0).
+ * mode 1 adds the twelve scale-factor copies of a GEMM K block before every
+ * four MMAs, from the MMA thread; mode 2 issues them from a second warp
+ * (modes 3-7 vary the copy shape and batching; mode 8 streams 32 KB bulk
+ * loads into shared memory beside the MMAs, mode 9 = modes 2 + 8, modes
+ * 10-12 add the GEMM's five-slot ring hand-off).  iters: a multiple of 4.  cycles (device, optional, 4
+ * entries): SM cycles and globaltimer nanoseconds of the first pair's issue
+ * loop; for mode 8 also the first CTA's load-loop cycles and load count.
  * No counterpart in the reference (its FP4 GEMM is a library call). */
-int q2b_fp4_mma_peak(int iters, void* stream);
+int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream);
 
 #ifdef __cplusplus
 }
