@@ -456,6 +456,28 @@ __device__ __forceinline__ void tc_commit_pair_if(bool issue, uint64_t* bar) {
       : "memory");
 }
 
+__device__ __forceinline__ void tc_commit_pair_leader_if(bool issue, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\t.reg .pred q;\n\tmov.b16 m, 1;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar)), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_cp_32x128b_x4_pair_if(bool issue, uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
+// Bounded wait by a whole warp; the result is the same in every lane (false if
+// any lane's wait gave up), so the warp's control flow stays converged.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, code));
+}
+
 // Scale-factor copy into both CTAs' TMEM, each from its own shared memory.
 __device__ __forceinline__ void tmem_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");

@@ -401,7 +401,15 @@ struct Gemm2Cfg {
 #define Q2B_GEMM2_EPI_WARPS 16
 #endif
   static constexpr int kEpiWarps = Q2B_GEMM2_EPI_WARPS;  // 4 per TMEM lane quarter, 64 columns each
-  static constexpr int kSfWarps = kStages;  // copy warp w owns ring slot w
+#ifndef Q2B_GEMM2_SF_GROUPS
+#define Q2B_GEMM2_SF_GROUPS 2
+#endif
+  // Scale-copy warps: groups of three (A scales, B scales of columns 0-127,
+  // of columns 128-255) that take K blocks in turn.  Copies cost tensor-pipe
+  // time and a single warp issues them at ~76 cycles each, so one warp per K
+  // block would make each block's copies a ~900-cycle serial step.
+  static constexpr int kSfGroups = Q2B_GEMM2_SF_GROUPS;
+  static constexpr int kSfWarps = 3 * kSfGroups;
   static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
@@ -463,7 +471,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&sfready[s], 1);
+      mbar_init(&sfready[s], 3);
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * Cfg::kEpiWarps);
@@ -487,30 +495,26 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const uint32_t smem_base = smem_u32(smem);
 
+  // The producer, scale-copy and MMA warps run their loops with all 32 lanes
+  // converged and one lane issuing (predicated tcgen05 instructions, a short
+  // lane-0 block for the TMA): a loop run by one diverged lane pays for every
+  // branch, and the MMA issue rate drops to a third of the pipe's.
+  const bool lead = lane == 0;
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
-    if (lane == 0) {
-      int64_t it = 0;
-      bool ok = true;
-      for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
-        const int64_t tm = t / tiles_n, tn = t % tiles_n;
-        const int a_row = static_cast<int>(tm * 256 + rank * 128);
-        const int b_row = static_cast<int>(tn * 256 + rank * 128);
-        const int64_t sfa_chunk0 = (tm * 2 + rank) * n_kt;
-        const int64_t sfb_chunk0 = (tn * 2) * n_kt;
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
-          const int slot = static_cast<int>(it % Cfg::kStages);
-          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-          Q2B_T0
-          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
-          Q2B_TW
-#ifdef Q2B_GEMM_PROBE_TIMING
-          if (it >= Cfg::kStages) acc_lat += clock64() - vt_mma[slot];
-          vt_issue[slot] = clock64();
-#endif
-#ifdef Q2B_GEMM_PROBE_NO_TMA
-          if (true) { if (leader) mbar_arrive(&full[slot]); continue; }
-#endif
+    int64_t it = 0;
+    bool ok = true;
+    for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
+      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      const int a_row = static_cast<int>(tm * 256 + rank * 128);
+      const int b_row = static_cast<int>(tn * 256 + rank * 128);
+      const int64_t sfa_chunk0 = (tm * 2 + rank) * n_kt;
+      const int64_t sfb_chunk0 = (tn * 2) * n_kt;
+      for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+        const int slot = static_cast<int>(it % Cfg::kStages);
+        const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+        if (!warp_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+        if (lead) {
           uint8_t* st = smem + slot * Cfg::kStageBytes;
           const uint32_t bar = map_to_rank(smem_u32(&full[slot]), 0);
           if (leader) mbar_arrive_expect_tx(&full[slot], 2 * Cfg::kStageBytes);
@@ -524,45 +528,44 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
           tma_load_2d_pair(st + Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + 2048, &tmap_sfb, bar, 0,
                            static_cast<int>((sfb_chunk0 + n_kt + kb * 4) * 2));
         }
+        __syncwarp();
       }
-      // drain: every issued stage is released by the MMAs (or the watchdog tripped)
-      const int64_t issued = it;
-      for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
-        mbar_wait(&empty[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
     }
+    // drain: every issued stage is released by the MMAs (or the watchdog tripped)
+    const int64_t issued = it;
+    for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
+      warp_wait(&empty[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
   } else if (warp >= 2 && warp < Cfg::kEpiWarp0) {
     // ------------------------------------------------------------ scale copies (leader)
-    if (leader && lane == 0) {
-      const int me = warp - 2;
+    if (leader) {
+      const int me = warp - 2, part = me % 3, group = me / 3;
       const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
       const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
-      // copy warp `me` serves every K block that lands in ring slot `me`
+      // this warp's part of a K block: A scales into columns 4j, B scales of
+      // columns 0-127 into 16+8j, of columns 128-255 into 20+8j
+      const uint64_t src0 = part == 0 ? sfa_d0 : (part == 1 ? sfb_d0 : sfb_d0 + 128);
+      const uint32_t col0 = part == 0 ? 0 : (part == 1 ? 16 : 20);
+      const uint32_t col_step = part == 0 ? 4 : 8;
       const int64_t my_tiles = cluster_id < ntiles ? (ntiles - 1 - cluster_id) / nclusters + 1 : 0;
       const int64_t total = my_tiles * nkb;
-      const int slot = me;
-      const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
-      const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
-      for (int64_t i = me; i < total; i += Cfg::kStages) {
+      for (int64_t i = group; i < total; i += Cfg::kSfGroups) {
+        const int slot = static_cast<int>(i % Cfg::kStages);
         const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1;
         const int64_t kb = i % nkb;
-        Q2B_T0
-        if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) break;
-        Q2B_TW
+        if (!warp_wait(&full[slot], ph, kTimeoutTmaFull)) break;
         tc_fence_after();
+        const uint64_t src = src0 + ((slot * Cfg::kStageBytes) >> 4);
+        const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols + col0;
         const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-        for (int j = 0; j < nk; ++j) {
-          tmem_cp_32x128b_x4_pair(set + 4 * j, sfa_d0 + so + 32 * j);
-          tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + so + 32 * j);
-          tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + so + 128 + 32 * j);
-        }
-        tc_commit_pair_leader(&sfready[slot]);
+        for (int j = 0; j < nk; ++j) tmem_cp_32x128b_x4_pair_if(lead, set + col_step * j, src + 32 * j);
+        tc_commit_pair_leader_if(lead, &sfready[slot]);
       }
-      tc_commit_pair_leader(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
+      tc_commit_pair_leader_if(lead, drain);
+      warp_wait(drain, 0, kTimeoutProducer);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issue (leader, lane 0)
-    if (leader && lane == 0) {
+    // ------------------------------------------------------------ MMA issue (leader)
+    if (leader) {
       const uint32_t idesc = idesc_nvf4(256, 256);
       const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
       const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
@@ -572,36 +575,32 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       bool ok = true;
       for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters, ++tc) {
         const uint32_t bph = static_cast<uint32_t>(tc) & 1;
-#ifdef Q2B_GEMM_PROBE_TIMING
-        const long long _te = clock64();
-#endif
-        if (!mbar_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
-#ifdef Q2B_GEMM_PROBE_TIMING
-        acc_lat += clock64() - _te;
-#endif
+        if (!warp_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
         tc_fence_after();
         for (int64_t kb = 0; kb < nkb; ++kb) {
-          Q2B_T0
-          if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
-          Q2B_TW
-#ifdef Q2B_GEMM_PROBE_TIMING
-          vt_mma[slot] = clock64();
-#endif
+          if (!warp_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
           tc_fence_after();
           const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
           const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
-          const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-          for (int j = 0; j < nk; ++j)
-            umma_nvf4_pair(tmem, a_d0 + so + 2 * j, b_d0 + so + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
-                           (kb > 0 || j > 0) ? 1u : 0u);
-          tc_commit_pair(&empty[slot]);
+          const uint64_t a_d = a_d0 + so, b_d = b_d0 + so;
+          if (kb != nkb - 1 || tail_nk == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              umma_nvf4_pair_if(lead, tmem, a_d + 2 * j, b_d + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
+                                (kb > 0 || j > 0) ? 1u : 0u);
+          } else {
+            for (int j = 0; j < tail_nk; ++j)
+              umma_nvf4_pair_if(lead, tmem, a_d + 2 * j, b_d + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
+                                (kb > 0 || j > 0) ? 1u : 0u);
+          }
+          tc_commit_pair_if(lead, &empty[slot]);
           if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
         if (!ok) break;
-        tc_commit_pair(tfull);
+        tc_commit_pair_if(lead, tfull);
       }
-      tc_commit_pair_leader(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
+      tc_commit_pair_leader_if(lead, drain);
+      warp_wait(drain, 0, kTimeoutProducer);
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -697,7 +696,7 @@ struct PeakCfg {
   static constexpr uint32_t kUsedBytes = 1024 + kOpBytes + kSfBytes + kSinkBytes + 256;
   // more than half an SM's shared memory: one CTA per SM, so no two pairs share a tensor pipe
   static constexpr uint32_t kSmemBytes = kUsedBytes > 120 * 1024 ? kUsedBytes : 120 * 1024;
-  static constexpr int kThreads = 128;
+  static constexpr int kThreads = 192;
 };
 
 __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int iters, int mode, long long* cycles) {
@@ -708,7 +707,8 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
   uint64_t* sinkbar = drain + 1;
   uint64_t* rfull = drain + 2;
   uint64_t* rempty = rfull + 5;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + 5);
+  uint64_t* rissued = rempty + 5;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rissued + 5);
   const int warp = threadIdx.x >> 5;
   const uint32_t rank = cluster_ctarank();
   for (uint32_t i = threadIdx.x; i < PeakCfg::kOpBytes / 4; i += blockDim.x) {
@@ -720,10 +720,11 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
     smem[PeakCfg::kOpBytes + i] = static_cast<uint8_t>(0x30u + ((i * 7u) & 0xFu));  // 0.5 .. 1.875
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
-    mbar_init(drain, (mode == 2 || mode == 9 || mode == 12) ? 2 : 1);
+    mbar_init(drain, (mode == 2 || mode == 9 || mode == 12 || mode == 14 || mode == 16) ? 2 : (mode == 17 ? 4 : 1));
     for (int k = 0; k < 5; ++k) {
-      mbar_init(&rfull[k], 1);
+      mbar_init(&rfull[k], mode == 17 ? 3 : 1);
       mbar_init(&rempty[k], 1);
+      mbar_init(&rissued[k], 1);
     }
     mbar_init(sinkbar, 1);
     fence_barrier_init();
@@ -763,7 +764,83 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
         asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(set + 8 * j), "l"(d) : "memory");
     }
   };
-  if (mode == 13 && rank == 0 && warp == 1) {
+  if (mode == 15 && rank == 0 && warp == 1) {
+    // mode 15: the MMA warp (converged) issues each K block's twelve scale
+    // copies into one of five sets, then its four MMAs (same-thread order)
+    const bool lead = (threadIdx.x & 31) == 0;
+    const uint32_t idesc = idesc_nvf4(256, 256);
+    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
+    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
+    const long long c0 = clock64();
+    uint64_t g0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
+    for (int kb = 0; kb < iters / 4; ++kb) {
+      const int slot = kb % 5;
+      const uint32_t rs = tmem + 256 + 48 * slot;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, rs + 4 * j, rs + 16 + 8 * j,
+                          (kb > 0 || j > 0) ? 1u : 0u);
+      tc_commit_pair_if(lead, &rempty[slot]);
+    }
+    tc_commit_pair_leader_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
+    if (lead && cycles != nullptr && blockIdx.x == 0) {
+      uint64_t g1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
+      cycles[0] = clock64() - c0;
+      cycles[1] = static_cast<long long>(g1 - g0);
+    }
+  } else   if ((mode == 14 || mode == 16 || mode == 17) && rank == 0 && warp == 1) {
+    // mode 14: mode 12's ring (copies by a second warp, signalled by commit) with
+    // both warps converged
+    const bool lead = (threadIdx.x & 31) == 0;
+    const uint32_t idesc = idesc_nvf4(256, 256);
+    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
+    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
+    const long long c0 = clock64();
+    uint64_t g0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
+    long long w_full = 0, w_iss = 0, t_mma = 0;
+    for (int kb = 0; kb < iters / 4; ++kb) {
+      const int slot = kb % 5;
+      const long long t0 = clock64();
+      if (!warp_wait(&rfull[slot], (kb / 5) & 1, kTimeoutTmaFull)) break;
+      const long long t1 = clock64();
+      // mode 16: the next block's copies are queued before this block's MMAs
+      if (mode == 16 && kb + 1 < iters / 4 &&
+          !warp_wait(&rissued[(kb + 1) % 5], ((kb + 1) / 5) & 1, kTimeoutTmaFull))
+        break;
+      const long long t2 = clock64();
+      w_full += t1 - t0;
+      w_iss += t2 - t1;
+      tc_fence_after();
+      const uint32_t rs = tmem + 256 + 48 * slot;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, rs + 4 * j, rs + 16 + 8 * j,
+                          (kb > 0 || j > 0) ? 1u : 0u);
+      tc_commit_pair_if(lead, &rempty[slot]);
+      t_mma += clock64() - t2;
+    }
+    tc_commit_pair_leader_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
+    if (lead && cycles != nullptr && blockIdx.x == 0) {
+      uint64_t g1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
+      cycles[0] = clock64() - c0;
+      cycles[1] = static_cast<long long>(g1 - g0);
+      cycles[2] = w_full;
+      cycles[3] = w_iss;
+      cycles[6] = t_mma;
+    }
+  } else if (mode == 13 && rank == 0 && warp == 1) {
     // mode 13: mode 10's loop run by the whole warp, converged, one lane issuing
     const bool lead = (threadIdx.x & 31) == 0;
     const uint32_t set = tmem + 256;
@@ -850,6 +927,57 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
       cycles[2] = clock64() - c0;
       cycles[3] = n;
     }
+  } else if (mode == 17 && rank == 0 && warp >= 2 && warp <= 4) {
+    // mode 17: each K block's copies split over three warps (A scales, B scales
+    // of columns 0-127, of columns 128-255), each committing to the slot's barrier
+    const bool lead = (threadIdx.x & 31) == 0;
+    const int part = warp - 2;
+    long long t_issue = 0;
+    for (int kb = 0; kb < iters / 4; ++kb) {
+      const int slot = kb % 5;
+      if (!warp_wait(&rempty[slot], ((kb / 5) & 1) ^ 1, kTimeoutSmemEmpty)) break;
+      const long long t1 = clock64();
+      tc_fence_after();
+      const uint32_t rs = tmem + 256 + 48 * slot;
+      for (int j = 0; j < 4; ++j) {
+        if (part == 0) tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
+        if (part == 1) tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
+        if (part == 2) tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
+      }
+      tc_commit_pair_leader_if(lead, &rfull[slot]);
+      t_issue += clock64() - t1;
+    }
+    if (lead && part == 0 && cycles != nullptr && blockIdx.x == 0) cycles[5] = t_issue;
+    tc_commit_pair_leader_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
+  } else if ((mode == 14 || mode == 16) && rank == 0 && warp == 2) {
+    // mode 14: mode 12's copy thread as a converged warp
+    const bool lead = (threadIdx.x & 31) == 0;
+    long long w_empty = 0, t_issue = 0;
+    for (int kb = 0; kb < iters / 4; ++kb) {
+      const int slot = kb % 5;
+      const long long t0 = clock64();
+      if (!warp_wait(&rempty[slot], ((kb / 5) & 1) ^ 1, kTimeoutSmemEmpty)) break;
+      const long long t1 = clock64();
+      w_empty += t1 - t0;
+      tc_fence_after();
+      const uint32_t rs = tmem + 256 + 48 * slot;
+      for (int j = 0; j < 4; ++j) {
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
+        tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
+      }
+      tc_commit_pair_leader_if(lead, &rfull[slot]);
+      if (lead) mbar_arrive(&rissued[slot]);
+      __syncwarp();
+      t_issue += clock64() - t1;
+    }
+    if (lead && cycles != nullptr && blockIdx.x == 0) {
+      cycles[4] = w_empty;
+      cycles[5] = t_issue;
+    }
+    tc_commit_pair_leader_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
   } else if ((mode == 11 || mode == 12) && rank == 0 && threadIdx.x == 64) {
     for (int kb = 0; kb < iters / 4; ++kb) {
       const int slot = kb % 5;
