@@ -409,6 +409,7 @@ struct Gemm2Cfg {
   // time and a single warp issues them at ~76 cycles each, so one warp per K
   // block would make each block's copies a ~900-cycle serial step.
   static constexpr int kSfGroups = Q2B_GEMM2_SF_GROUPS;
+  static_assert(kSfGroups >= 1 && kSfGroups <= 3, "2 + 3 * kSfGroups + epilogue warps must fit the block");
   static constexpr int kSfWarps = 3 * kSfGroups;
   static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
@@ -548,11 +549,16 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       const uint32_t col_step = part == 0 ? 4 : 8;
       const int64_t my_tiles = cluster_id < ntiles ? (ntiles - 1 - cluster_id) / nclusters + 1 : 0;
       const int64_t total = my_tiles * nkb;
-      for (int64_t i = group; i < total; i += Cfg::kSfGroups) {
+      // Every copy warp waits for every K block's stage in order, copying only
+      // for its own group's blocks: a parity wait is only unambiguous when the
+      // previous phase of that barrier is known to be complete, and TMA loads
+      // of different stages may land out of order.
+      for (int64_t i = 0; i < total; ++i) {
         const int slot = static_cast<int>(i % Cfg::kStages);
         const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1;
         const int64_t kb = i % nkb;
         if (!warp_wait(&full[slot], ph, kTimeoutTmaFull)) break;
+        if (i % Cfg::kSfGroups != group) continue;
         tc_fence_after();
         const uint64_t src = src0 + ((slot * Cfg::kStageBytes) >> 4);
         const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols + col0;
