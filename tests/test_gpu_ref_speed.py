@@ -1,6 +1,6 @@
 """Same-box timing of the reference's own GPU path against ours on the four 4B linears
-(SURVEY.md-style "reference GPU baseline", BASELINE config 3 at 16384 tokens to keep the
-test short): the reference's quantizer kernels built from its sources (oracle/_ref/libq2ref.so,
+(the "reference GPU baseline" of the 4B linear-set workload, at 16384 tokens by default to keep
+the test short; Q2B_REF_SPEED_TOKENS sets another count): the reference's quantizer kernels built from its sources (oracle/_ref/libq2ref.so,
 see oracle/Makefile) plus FlashInfer's cuDNN NVFP4 GEMM, composed as Quartet_II_fn does
 (quartet2/python/quartet2/linear.py:155-233), against cloverlm_b200's kernels.  Prints the
 per-op table (run with -s); asserts only that both paths ran and ours is not slower than 1.5x."""
@@ -75,7 +75,7 @@ def test_reference_gpu_path_vs_ours():
                       use_8x4_sf_layout=False, backend="cudnn", use_nvfp4=True)
 
     h = get_hadamard_matrix(128, torch.bfloat16, "cuda")[:16].contiguous()
-    M = 16384
+    M = int(os.environ.get("Q2B_REF_SPEED_TOKENS", "16384"))
     tot = {"ref": 0.0, "ours": 0.0}
     rows = []
     for name, K, N in SHAPES:
