@@ -1,7 +1,7 @@
 """Same-box timing of the reference's own GPU path against ours on the four 4B linears
 (the "reference GPU baseline" of the 4B linear-set workload, at 16384 tokens by default to keep
-the test short; Q2B_REF_SPEED_TOKENS sets another count): the reference's quantizer kernels built from its sources (oracle/_ref/libq2ref.so,
-see oracle/Makefile) plus FlashInfer's cuDNN NVFP4 GEMM, composed as Quartet_II_fn does
+the test short; Q2B_REF_SPEED_TOKENS sets another count): the reference's quantizer kernels
+built from its sources (oracle/_ref/libq2ref.so, see oracle/Makefile) plus FlashInfer's cuDNN NVFP4 GEMM, composed as Quartet_II_fn does
 (quartet2/python/quartet2/linear.py:155-233), against cloverlm_b200's kernels.  Prints the
 per-op table (run with -s); asserts only that both paths ran and ours is not slower than 1.5x."""
 import ctypes
