@@ -472,6 +472,21 @@ __device__ __forceinline__ void tmem_cp_32x128b_x4_pair_if(bool issue, uint32_t 
       : "memory");
 }
 
+// TMA tensor store shared -> global of one box at (x, y), tracked as a bulk
+// group of the issuing thread (no multicast; the destination is local memory).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until the thread's bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Bounded wait by a whole warp; the result is the same in every lane (false if
 // any lane's wait gave up), so the warp's control flow stays converged.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned code) {

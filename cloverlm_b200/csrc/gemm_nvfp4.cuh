@@ -413,8 +413,24 @@ struct Gemm2Cfg {
   static constexpr int kSfWarps = 3 * kSfGroups;
   static constexpr int kEpiWarp0 = 2 + kSfWarps;
   static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
-  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + 512;
+  // epilogue staging after the ring and the barriers: 2 KB per epilogue warp
+  static constexpr uint32_t kStagingPerWarp = 32 * 32 * 2;
+  static constexpr uint32_t kStagingOff = (kStages * kStageBytes + 512 + 1023) / 1024 * 1024;
+  static constexpr uint32_t kSmemBytes = 1024 + kStagingOff + kEpiWarps * kStagingPerWarp;
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
+
+#ifdef Q2B_GEMM2_STATS
+// Instrumented builds only: cycle counts of CTA 0's roles (0 MMA: total, 1 MMA: waiting for
+// scales, 2 MMA: waiting for the accumulator, 3 K blocks, 4 copy warp 0: waiting for stages,
+// 5 producer: waiting for free slots, 6 epilogue warp 0: waiting for tiles, 7 tiles).
+__device__ long long g_gemm2_stats[8];
+#define Q2B_S_T(v) const long long v = clock64();
+#define Q2B_S_ADD(i, val) if (blockIdx.x == 0 && lane == 0) g_gemm2_stats[i] += (val);
+#else
+#define Q2B_S_T(v)
+#define Q2B_S_ADD(i, val)
+#endif
 
 // Arrive on the leader CTA's copy of `bar` when this thread's prior 2-CTA
 // tcgen05 ops complete.
@@ -435,7 +451,7 @@ __device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
 __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const GemmParams p) {
+                          const __grid_constant__ CUtensorMap tmap_d, const GemmParams p) {
   using Cfg = Gemm2Cfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -448,17 +464,6 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#ifdef Q2B_GEMM_PROBE_TIMING
-  __shared__ long long t_issue[Gemm2Cfg::kStages], t_mma[Gemm2Cfg::kStages];
-  volatile long long* vt_issue = t_issue;
-  volatile long long* vt_mma = t_mma;
-  long long acc_wait = 0, acc_lat = 0, nacc = 0;
-#define Q2B_T0 const long long _t0 = clock64();
-#define Q2B_TW acc_wait += clock64() - _t0; ++nacc;
-#else
-#define Q2B_T0
-#define Q2B_TW
-#endif
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -514,7 +519,9 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
         const int slot = static_cast<int>(it % Cfg::kStages);
         const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+        Q2B_S_T(_p0)
         if (!warp_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+        Q2B_S_ADD(5, clock64() - _p0)
         if (lead) {
           uint8_t* st = smem + slot * Cfg::kStageBytes;
           const uint32_t bar = map_to_rank(smem_u32(&full[slot]), 0);
@@ -557,7 +564,9 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         const int slot = static_cast<int>(i % Cfg::kStages);
         const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1;
         const int64_t kb = i % nkb;
+        Q2B_S_T(_c0)
         if (!warp_wait(&full[slot], ph, kTimeoutTmaFull)) break;
+        if (me == 0) { Q2B_S_ADD(4, clock64() - _c0) }
         if (i % Cfg::kSfGroups != group) continue;
         tc_fence_after();
         const uint64_t src = src0 + ((slot * Cfg::kStageBytes) >> 4);
@@ -579,12 +588,18 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       uint32_t ph = 0;
       int64_t tc = 0;
       bool ok = true;
+      Q2B_S_T(_m00)
       for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters, ++tc) {
         const uint32_t bph = static_cast<uint32_t>(tc) & 1;
+        Q2B_S_T(_m0)
         if (!warp_wait(tempty, bph ^ 1, kTimeoutTmemEmpty)) break;
+        Q2B_S_ADD(2, clock64() - _m0)
         tc_fence_after();
         for (int64_t kb = 0; kb < nkb; ++kb) {
+          Q2B_S_T(_m1)
           if (!warp_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+          Q2B_S_ADD(1, clock64() - _m1)
+          Q2B_S_ADD(3, 1)
           tc_fence_after();
           const uint64_t so = (slot * Cfg::kStageBytes) >> 4;
           const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
@@ -605,35 +620,33 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         if (!ok) break;
         tc_commit_pair_if(lead, tfull);
       }
+      Q2B_S_ADD(0, clock64() - _m00)
       tc_commit_pair_leader_if(lead, drain);
       warp_wait(drain, 0, kTimeoutProducer);
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    // Each warp drains its 32 rows x 64 columns with one TMEM round trip,
+    // releases the accumulator, then scales to bf16 and writes two 32 x 32
+    // boxes through its 2 KB staging buffer (64-byte swizzle) with TMA
+    // stores: coalesced writes, where per-lane 16-byte row stores slowed the
+    // whole mainloop (a third of the forward GEMM's time at K = 3584).
     const int e = warp - Cfg::kEpiWarp0;
     const int q = warp & 3;
     constexpr int kCols = 256 / (Cfg::kEpiWarps / 4);  // columns per warp
     const int c0 = (e >> 2) * kCols;
     const float alpha = *p.alpha * (p.alpha_b != nullptr ? *p.alpha_b : 1.f);
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
+    uint8_t* stage = smem + Cfg::kStagingOff + e * Cfg::kStagingPerWarp;
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
-#ifdef Q2B_GEMM_PROBE_TIMING
-      const long long _tf = clock64();
-#endif
+      Q2B_S_T(_e0)
       if (!mbar_wait(tfull, static_cast<uint32_t>(tc) & 1, kTimeoutTmemFull)) break;
-#ifdef Q2B_GEMM_PROBE_TIMING
-      const long long _tg = clock64();
-      acc_wait += _tg - _tf;
-      ++nacc;
-#endif
+      if (e == 0) { Q2B_S_ADD(6, clock64() - _e0) Q2B_S_ADD(7, 1) }
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
-      const int64_t row = tm * 256 + rank * 128 + q * 32 + lane;
-      __nv_bfloat16* drow = p.D + row * p.N + tn * 256 + c0;
+      const int row0 = static_cast<int>(tm * 256 + rank * 128 + q * 32);
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
-      // One TMEM round trip for the warp's whole slice, then the accumulator
-      // goes back to the MMA warp; scaling, packing and stores follow.
       uint32_t r[kCols / 32][32];
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
@@ -641,25 +654,29 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-#ifdef Q2B_GEMM_PROBE_TIMING
-      acc_lat += clock64() - _tg;
-#endif
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) {
         uint32_t o[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k)
           o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
-#ifdef Q2B_GEMM_PROBE_NO_STORE
-        if (o[0] == 0x12345678u)
-#endif
-        {
-          uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+        // the previous box's store must have read the staging buffer
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        for (int k = 0; k < 4; ++k)  // 16-byte chunk k of row `lane`, 64-byte swizzle
+          *reinterpret_cast<uint4*>(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_d, stage, static_cast<int>(tn * 256 + c0 + ch * 32), row0);
+          bulk_commit_group();
         }
       }
     }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -591,9 +591,12 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
                     static_cast<__nv_bfloat16*>(D), m_valid, 1, nullptr, nullptr};
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
-  if (m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms) {
-    // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair
-    CUtensorMap tsa, tsb;
+  if (m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms &&
+      (reinterpret_cast<uintptr_t>(D) & 15u) == 0) {
+    // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair; D written by TMA stores
+    CUtensorMap tsa, tsb, td;
+    if (int r = make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return r;
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
     if (int r = make_tmap(&tsa, sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, M * K / 16 / 256, 256, 8,
                           CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -615,7 +618,7 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel, ta, tb, tsa, tsb, p));
+    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel, ta, tb, tsa, tsb, td, p));
     return Q2B_OK;
   }
 #endif
@@ -703,5 +706,15 @@ int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
   Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters, mode, cycles));
   return Q2B_OK;
 }
+
+#ifdef Q2B_GEMM2_STATS
+// Instrumented builds only: read and clear the pair GEMM's cycle counters.
+int q2b_gemm2_stats(long long* out) {
+  Q2B_CUDA(cudaMemcpyFromSymbol(out, q2b::g_gemm2_stats, sizeof(long long) * 8));
+  long long zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  Q2B_CUDA(cudaMemcpyToSymbol(q2b::g_gemm2_stats, zero, sizeof(zero)));
+  return Q2B_OK;
+}
+#endif
 
 }  // extern "C"
