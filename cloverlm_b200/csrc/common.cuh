@@ -487,6 +487,35 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 // Wait until the thread's bulk stores have completed.
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 1-CTA forms of the predicated issue helpers.
+__device__ __forceinline__ void umma_nvf4_if(bool issue, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "setp.ne.b32 q, %7, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_if(bool issue, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_cp_32x128b_x4_if(bool issue, uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc), "r"(issue ? 1u : 0u)
+      : "memory");
+}
+
 // Bounded wait by a whole warp; the result is the same in every lane (false if
 // any lane's wait gave up), so the warp's control flow stays converged.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned code) {

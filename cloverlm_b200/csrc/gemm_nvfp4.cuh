@@ -127,21 +127,22 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const uint32_t smem_base = smem_u32(smem);
 
+  // Producer, scale-copy and MMA loops run on converged warps with one lane
+  // issuing (predicated tcgen05 instructions, a short lane-0 block for the
+  // loads): a loop run by one diverged lane pays for every branch.
+  const bool lead = lane == 0;
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int64_t it = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-        const int64_t t = u / splits, sp = u % splits;
-        const int64_t tm = t / tiles_n, tn = t % tiles_n;
-        for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb, ++it) {
-          const int slot = static_cast<int>(it % Cfg::kStages);
-          const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
-          if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
-#ifdef Q2B_GEMM_PROBE_NO_TMA
-          if (true) { mbar_arrive(&full[slot]); continue; }
-#endif
+    int64_t it = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      const int64_t t = u / splits, sp = u % splits;
+      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb, ++it) {
+        const int slot = static_cast<int>(it % Cfg::kStages);
+        const uint32_t ph = static_cast<uint32_t>(it / Cfg::kStages) & 1;
+        if (!warp_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) { ok = false; break; }
+        if (lead) {
           const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
           uint8_t* st = smem + slot * Cfg::kStageBytes;
           const uint32_t sf_bytes = nk * 512u;
@@ -151,103 +152,93 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
                       static_cast<int>(tn * BN));
           bulk_load(st + Cfg::kABytes + Cfg::kBBytes, p.sfa + ((tm * n_kt + kb * 4) << 9), sf_bytes, &full[slot]);
 #pragma unroll
-          for (int u = 0; u < BN / 128; ++u)
-            bulk_load(st + Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + u * 2048,
-                      p.sfb + (((tn * (BN / 128) + u) * n_kt + kb * 4) << 9), sf_bytes, &full[slot]);
+          for (int v = 0; v < BN / 128; ++v)
+            bulk_load(st + Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + v * 2048,
+                      p.sfb + (((tn * (BN / 128) + v) * n_kt + kb * 4) << 9), sf_bytes, &full[slot]);
         }
+        __syncwarp();
       }
-      const int64_t issued = it;
-      for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
-        mbar_wait(&full[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
     }
+    const int64_t issued = it;
+    for (int64_t k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
+      warp_wait(&full[k % Cfg::kStages], static_cast<uint32_t>(k / Cfg::kStages) & 1, kTimeoutProducer);
   } else if (warp >= 2 && warp < 2 + Cfg::kSfWarps) {
     // ------------------------------------------------------------ scale copies
     const int me = warp - 2;
     constexpr int kPerStep = 1 + BN / 128;
-    if (lane == 0) {
-      // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
-      const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
-      const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
-      int slot = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-        const int64_t sp = u % splits;
-        for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb) {
-          if (!mbar_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
-          tc_fence_after();
-          const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
-          const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
-          const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
-#ifndef Q2B_GEMM_PROBE_NO_SFCP
-          // copies in TMEM column order (A steps, then B steps x halves);
-          // each warp takes a contiguous block of them
-          const int ncp = nk * kPerStep;
-          const int lo = me * ncp / Cfg::kSfWarps, hi = (me + 1) * ncp / Cfg::kSfWarps;
-          for (int c = lo; c < hi; ++c) {
-            if (c < nk) {
-              tmem_cp_32x128b_x4(set + 4 * c, sfa_d0 + so + 32 * c);
-            } else {
-              const int b = c - nk, j = b / (BN / 128), u = b % (BN / 128);
-              tmem_cp_32x128b_x4(set + 16 + (BN / 32) * j + 4 * u, sfb_d0 + so + 128 * u + 32 * j);
-            }
+    // descriptors of stage 0's scale chunks; stage s adds s * kStageBytes
+    const uint64_t sfa_d0 = smem_desc(smem_base + Cfg::kABytes + Cfg::kBBytes, 0, 128, kLayoutNone);
+    const uint64_t sfb_d0 = sfa_d0 + (Cfg::kSfaBytes >> 4);
+    int slot = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      const int64_t sp = u % splits;
+      for (int64_t kb = sp * nkb / splits; kb < (sp + 1) * nkb / splits; ++kb) {
+        if (!warp_wait(&full[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
+        tc_fence_after();
+        const int nk = (kb == nkb - 1 && tail_nk) ? tail_nk : 4;
+        const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
+        const uint32_t set = tmem + Cfg::kSfBase + slot * Cfg::kSfSetCols;
+        // copies in TMEM column order (A steps, then B steps x halves);
+        // each warp takes a contiguous block of them
+        const int ncp = nk * kPerStep;
+        const int lo = me * ncp / Cfg::kSfWarps, hi = (me + 1) * ncp / Cfg::kSfWarps;
+        for (int c = lo; c < hi; ++c) {
+          if (c < nk) {
+            tmem_cp_32x128b_x4_if(lead, set + 4 * c, sfa_d0 + so + 32 * c);
+          } else {
+            const int b = c - nk, j = b / (BN / 128), v = b % (BN / 128);
+            tmem_cp_32x128b_x4_if(lead, set + 16 + (BN / 32) * j + 4 * v, sfb_d0 + so + 128 * v + 32 * j);
           }
-#else
-          (void)nk; (void)so; (void)set;
-#endif
-          tc_commit(&sfready[slot]);
-          if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
         }
+        tc_commit_if(lead, &sfready[slot]);
+        if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
       }
-      tc_commit(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
     }
+    tc_commit_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    // tcgen05.mma issue blocks until the pipe can take it, so the issuing
-    // thread keeps its loop minimal: lane 0 alone, incremental slot/phase,
-    // precomputed descriptors, no warp-wide sync per K block.
-    if (lane == 0) {
-      const uint32_t idesc = idesc_nvf4(Cfg::BM, BN);
-      const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
-      const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
-      const uint32_t sf0 = tmem + Cfg::kSfBase;
-      int slot = 0;
-      uint32_t ph = 0;
-      int64_t tc = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++tc) {
-        const int buf = static_cast<int>(tc % Cfg::kAccBufs);
-        const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
-        if (!mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty)) break;
+    const uint32_t idesc = idesc_nvf4(Cfg::BM, BN);
+    const uint64_t a_d0 = smem_desc(smem_base, 0, 1024, kLayoutSW128);
+    const uint64_t b_d0 = smem_desc(smem_base + Cfg::kABytes, 0, 1024, kLayoutSW128);
+    const uint32_t sf0 = tmem + Cfg::kSfBase;
+    int slot = 0;
+    uint32_t ph = 0;
+    int64_t tc = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++tc) {
+      const int buf = static_cast<int>(tc % Cfg::kAccBufs);
+      const uint32_t bph = static_cast<uint32_t>(tc / Cfg::kAccBufs) & 1;
+      if (!warp_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * BN;
+      const int64_t sp = u % splits, kb0 = sp * nkb / splits;
+      for (int64_t kb = kb0; kb < (sp + 1) * nkb / splits; ++kb) {
+        if (!warp_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
-        const int64_t sp = u % splits, kb0 = sp * nkb / splits;
-        for (int64_t kb = kb0; kb < (sp + 1) * nkb / splits; ++kb) {
-          if (!mbar_wait(&sfready[slot], ph, kTimeoutTmaFull)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
-          const uint32_t set = sf0 + slot * Cfg::kSfSetCols;
-          const uint64_t ad = a_d0 + so, bd = b_d0 + so;
-          if (kb == nkb - 1 && tail_nk) {
-            for (int j = 0; j < tail_nk; ++j)
-              umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
-                        (kb > kb0 || j > 0) ? 1u : 0u);
-          } else {
-            umma_nvf4(d, ad, bd, idesc, set, set + 16, kb > kb0 ? 1u : 0u);
+        const uint64_t so = static_cast<uint64_t>((slot * Cfg::kStageBytes) >> 4);
+        const uint32_t set = sf0 + slot * Cfg::kSfSetCols;
+        const uint64_t ad = a_d0 + so, bd = b_d0 + so;
+        if (kb == nkb - 1 && tail_nk) {
+          for (int j = 0; j < tail_nk; ++j)
+            umma_nvf4_if(lead, d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
+                         (kb > kb0 || j > 0) ? 1u : 0u);
+        } else {
 #pragma unroll
-            for (int j = 1; j < 4; ++j)
-              umma_nvf4(d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j, 1u);
-          }
-          tc_commit(&empty[slot]);
-          if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
+          for (int j = 0; j < 4; ++j)
+            umma_nvf4_if(lead, d, ad + 2 * j, bd + 2 * j, idesc, set + 4 * j, set + 16 + (BN / 32) * j,
+                         (kb > kb0 || j > 0) ? 1u : 0u);
         }
-        if (!ok) break;
-        tc_commit(&tfull[buf]);
+        tc_commit_if(lead, &empty[slot]);
+        if (++slot == Cfg::kStages) { slot = 0; ph ^= 1; }
       }
-      tc_commit(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
+      if (!ok) break;
+      tc_commit_if(lead, &tfull[buf]);
     }
+    tc_commit_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
   } else {
     // ------------------------------------------------------------ epilogue
     const int e = warp - Cfg::kEpiWarp0;
