@@ -414,10 +414,12 @@ struct Gemm2Cfg {
 #ifdef Q2B_GEMM2_STATS
 // Instrumented builds only: cycle counts of CTA 0's roles (0 MMA: total, 1 MMA: waiting for
 // scales, 2 MMA: waiting for the accumulator, 3 K blocks, 4 copy warp 0: waiting for stages,
-// 5 producer: waiting for free slots, 6 epilogue warp 0: waiting for tiles, 7 tiles).
-__device__ long long g_gemm2_stats[8];
+// 5 producer: waiting for free slots, 6 epilogue warp 0: waiting for tiles, 7 tiles,
+// 8 / 9 epilogue warp 0: issuing / waiting for its TMEM loads).  Counted in registers and
+// added to the global counters once at exit, so the counting stays off the timed paths.
+__device__ long long g_gemm2_stats[10];
 #define Q2B_S_T(v) const long long v = clock64();
-#define Q2B_S_ADD(i, val) if (blockIdx.x == 0 && lane == 0) g_gemm2_stats[i] += (val);
+#define Q2B_S_ADD(i, val) q2b_st[i] += (val);
 #else
 #define Q2B_S_T(v)
 #define Q2B_S_ADD(i, val)
@@ -455,6 +457,9 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef Q2B_GEMM2_STATS
+  long long q2b_st[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+#endif
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -634,6 +639,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       Q2B_S_T(_e0)
       if (!mbar_wait(tfull, static_cast<uint32_t>(tc) & 1, kTimeoutTmemFull)) break;
       if (e == 0) { Q2B_S_ADD(6, clock64() - _e0) Q2B_S_ADD(7, 1) }
+      Q2B_S_T(_e1)
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
       const int row0 = static_cast<int>(tm * 256 + rank * 128 + q * 32);
@@ -641,10 +647,12 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       uint32_t r[kCols / 32][32];
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
+      Q2B_S_T(_e2)
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
+      if (e == 0) { Q2B_S_ADD(8, _e2 - _e1) Q2B_S_ADD(9, clock64() - _e2) }
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) {
         uint32_t o[16];
@@ -670,6 +678,12 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     __syncwarp();
   }
 
+#ifdef Q2B_GEMM2_STATS
+  if (blockIdx.x == 0 && lane == 0)
+    for (int i = 0; i < 10; ++i)
+      if (q2b_st[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&g_gemm2_stats[i]),
+                                    static_cast<unsigned long long>(q2b_st[i]));
+#endif
   tc_fence_before();
   cluster_sync();
   if (warp == 1) {
