@@ -688,7 +688,7 @@ int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, co
 
 int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
   if (iters <= 0 || iters % 4 != 0 || iters > (1 << 24)) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: iters must be a positive multiple of 4 up to 2^24");
-  if (mode < 0 || mode > 18) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: mode must be 0 .. 18");
+  if (mode < 0 || mode > 17) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: mode must be 0 .. 17");
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaLaunchConfig_t cfg = {};
