@@ -192,10 +192,14 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
  * mode 1 adds the twelve scale-factor copies of a GEMM K block before every
  * four MMAs, from the MMA thread; mode 2 issues them from a second warp
  * (modes 3-7 vary the copy shape and batching; mode 8 streams 32 KB bulk
- * loads into shared memory beside the MMAs, mode 9 = modes 2 + 8, modes
- * 10-12 add the GEMM's five-slot ring hand-off).  iters: a multiple of 4.  cycles (device, optional, 4
+ * loads into shared memory beside the MMAs, mode 9 = modes 2 + 8; modes
+ * 10-12 add the GEMM's five-slot ring hand-off from one diverged lane,
+ * 13 is mode 10's loop on a converged warp, 14 / 16 / 17 the ring with the
+ * copy warp(s) converged, 15 the copies issued by the MMA warp itself).
+ * iters: a multiple of 4; mode 0 .. 17.  cycles (device, optional, 8
  * entries): SM cycles and globaltimer nanoseconds of the first pair's issue
- * loop; for mode 8 also the first CTA's load-loop cycles and load count.
+ * loop; mode 8 adds the first CTA's load-loop cycles and load count, modes
+ * 14/16 per-role wait and issue cycles.
  * No counterpart in the reference (its FP4 GEMM is a library call). */
 int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream);
 

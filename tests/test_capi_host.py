@@ -97,6 +97,13 @@ def test_adamw_rejects_bad_arguments():
         _lib.call("q2b_adamw_step", None, FAKE, FAKE, FAKE, 0, 8, 1e-3, 0.9, 0.99, 1e-8, 0.0, 1, None, None, None)
 
 
+def test_fp4_mma_peak_rejects_bad_arguments():
+    with pytest.raises(ValueError, match="multiple of 4"):
+        _lib.call("q2b_fp4_mma_peak", 6, 0, None, None)
+    with pytest.raises(ValueError, match="mode must be"):
+        _lib.call("q2b_fp4_mma_peak", 64, 18, None, None)
+
+
 def test_last_error_is_thread_local_text():
     with pytest.raises(ValueError):
         _lib.call("q2b_gemm_nvfp4", FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100, 128, 128, None)
