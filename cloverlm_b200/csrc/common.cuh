@@ -387,6 +387,19 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Relaxed arrive: no release of the thread's prior memory operations.  For a
+// hand-off of tensor memory only (the reads already completed by
+// tcgen05.wait::ld, ordered by tcgen05.fence::before_thread_sync), where a
+// cluster-scope release would wait ~2 k cycles for the warp's outstanding
+// stores.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // TMA tile load into this CTA's shared memory whose completion is counted on
 // an mbarrier that may live in either CTA of the pair (`bar_cluster`).
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int x, int y) {

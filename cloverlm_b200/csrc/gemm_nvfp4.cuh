@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
+          if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
           float* wrow = p.ws + t * (Cfg::BM * BN) + trow * BN + c0;
           if (live) {
 #pragma unroll
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
       if (live) {
 #pragma unroll
         for (int ch = 0; ch < kChunks; ++ch) {
@@ -417,7 +417,7 @@ struct Gemm2Cfg {
 // 5 producer: waiting for free slots, 6 epilogue warp 0: waiting for tiles, 7 tiles,
 // 8 / 9 epilogue warp 0: issuing / waiting for its TMEM loads).  Counted in registers and
 // added to the global counters once at exit, so the counting stays off the timed paths.
-__device__ long long g_gemm2_stats[10];
+__device__ long long g_gemm2_stats[12];
 #define Q2B_S_T(v) const long long v = clock64();
 #define Q2B_S_ADD(i, val) q2b_st[i] += (val);
 #else
@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #ifdef Q2B_GEMM2_STATS
-  long long q2b_st[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  long long q2b_st[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
 #endif
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -636,23 +636,28 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     uint8_t* stage = smem + Cfg::kStagingOff + e * Cfg::kStagingPerWarp;
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
+      // tile coordinates before the wait: the drain is on the MMA's critical path
+      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      const int row0 = static_cast<int>(tm * 256 + rank * 128 + q * 32);
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
       Q2B_S_T(_e0)
       if (!mbar_wait(tfull, static_cast<uint32_t>(tc) & 1, kTimeoutTmemFull)) break;
       if (e == 0) { Q2B_S_ADD(6, clock64() - _e0) Q2B_S_ADD(7, 1) }
       Q2B_S_T(_e1)
       tc_fence_after();
-      const int64_t tm = t / tiles_n, tn = t % tiles_n;
-      const int row0 = static_cast<int>(tm * 256 + rank * 128 + q * 32);
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
       uint32_t r[kCols / 32][32];
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) tmem_ld_32x32b_x32(taddr + ch * 32, r[ch]);
       Q2B_S_T(_e2)
       tmem_ld_wait();
+      Q2B_S_T(_e3)
       tc_fence_before();
+      Q2B_S_T(_e4)
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      if (e == 0) { Q2B_S_ADD(8, _e2 - _e1) Q2B_S_ADD(9, clock64() - _e2) }
+      Q2B_S_T(_e5)
+      // relaxed: only tensor memory changes hands, its reads already complete
+      if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader);
+      if (e == 0) { Q2B_S_ADD(8, _e2 - _e1) Q2B_S_ADD(9, _e3 - _e2) Q2B_S_ADD(10, _e4 - _e3) Q2B_S_ADD(11, _e5 - _e4) }
 #pragma unroll
       for (int ch = 0; ch < kCols / 32; ++ch) {
         uint32_t o[16];
@@ -680,7 +685,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
 
 #ifdef Q2B_GEMM2_STATS
   if (blockIdx.x == 0 && lane == 0)
-    for (int i = 0; i < 10; ++i)
+    for (int i = 0; i < 12; ++i)
       if (q2b_st[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&g_gemm2_stats[i]),
                                     static_cast<unsigned long long>(q2b_st[i]));
 #endif

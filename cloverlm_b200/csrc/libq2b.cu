@@ -710,8 +710,8 @@ int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
 #ifdef Q2B_GEMM2_STATS
 // Instrumented builds only: read and clear the pair GEMM's cycle counters.
 int q2b_gemm2_stats(long long* out) {
-  Q2B_CUDA(cudaMemcpyFromSymbol(out, q2b::g_gemm2_stats, sizeof(long long) * 10));
-  long long zero[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  Q2B_CUDA(cudaMemcpyFromSymbol(out, q2b::g_gemm2_stats, sizeof(long long) * 12));
+  long long zero[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
   Q2B_CUDA(cudaMemcpyToSymbol(q2b::g_gemm2_stats, zero, sizeof(zero)));
   return Q2B_OK;
 }

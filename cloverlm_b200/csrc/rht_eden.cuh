@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         if (ch == kNChunks - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
+          if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
         }
         uint32_t cw[2 * kG], fs[kG];
 #ifdef Q2B_RHT_PROBE_NO_EPI
