@@ -717,4 +717,14 @@ int q2b_gemm2_stats(long long* out) {
 }
 #endif
 
+#ifdef Q2B_RHT_STATS
+// Instrumented builds only: read and clear the RHT/EDEN kernel's cycle counters.
+int q2b_rht_stats(long long* out) {
+  Q2B_CUDA(cudaMemcpyFromSymbol(out, q2b::g_rht_stats, sizeof(long long) * 12));
+  long long zero[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  Q2B_CUDA(cudaMemcpyToSymbol(q2b::g_rht_stats, zero, sizeof(zero)));
+  return Q2B_OK;
+}
+#endif
+
 }  // extern "C"

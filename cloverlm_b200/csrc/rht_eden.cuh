@@ -150,6 +150,19 @@ __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, ui
   return __uint_as_float(hb << 16);
 }
 
+#ifdef Q2B_RHT_STATS
+// Instrumented builds only: cycle counts of CTA 0 of the last launch's roles (0 producer warp 0:
+// waiting for a free stage, 1: converting, 2: loop total; 3 MMA: waiting for a TMEM buffer,
+// 4: waiting for a stage, 5: loop total, 6: tiles; 7 epilogue warp 0: waiting for its tile,
+// 8: TMEM loads, 9: EDEN and stores, 10: loop total).  Counted in registers, added at exit.
+__device__ long long g_rht_stats[12];
+#define Q2B_R_T(v) const long long v = clock64();
+#define Q2B_R_ADD(i, val) q2b_rs[i] += (val);
+#else
+#define Q2B_R_T(v)
+#define Q2B_R_ADD(i, val)
+#endif
+
 template <int kIn, int kOut>
 __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     rht_eden_kernel(const __grid_constant__ CUtensorMap tmap_x, const RhtParams p) {
@@ -168,6 +181,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles_n = p.N >> 7;
   const int64_t ntiles = (p.M >> 7) * tiles_n;
+#ifdef Q2B_RHT_STATS
+  long long q2b_rs[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRhtStages; ++s) {
@@ -250,7 +266,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       auto convert = [&](int it, const uint4 (&qc)[kItems], const uint32_t (&sc)[kItems]) -> bool {
         const int slot = it % kRhtStages;
         const uint32_t ph = (it / kRhtStages) & 1;
+        Q2B_R_T(_p0)
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
+        Q2B_R_T(_p1)
+        Q2B_R_ADD(0, _p1 - _p0)
         uint8_t* dst = tiles + slot * kTileBytes;
 #ifdef Q2B_RHT_PROBE_NO_CONVERT
         if (true) { fence_proxy_async_smem(); mbar_arrive(&full[slot]); return true; }
@@ -279,9 +298,11 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&full[slot]);
+        Q2B_R_ADD(1, clock64() - _p1)
         return true;
       };
       const int64_t step = gridDim.x;
+      Q2B_R_T(_pl)
       int64_t t = blockIdx.x;
       if (t < ntiles) load_tile(t, qa, sa);
       if (t + step < ntiles) load_tile(t + step, qb, sbb);
@@ -303,6 +324,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         t += step;
         ++it;
       }
+      Q2B_R_ADD(2, clock64() - _pl)
     }
   } else if (warp == Cfg::kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
@@ -311,12 +333,19 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     const uint32_t hs_addr = smem_u32(hs);
     int it = 0;
     bool ok = true;
+    Q2B_R_T(_ml)
     for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
       const int slot = it % kRhtStages;
       const uint32_t ph = (it / kRhtStages) & 1;
       const int buf = it % Cfg::kEpiGroups;
       const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
-      ok = mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty) && mbar_wait(&full[slot], ph, kTimeoutTmaFull);
+      Q2B_R_T(_m0)
+      ok = mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty);
+      Q2B_R_T(_m1)
+      ok = ok && mbar_wait(&full[slot], ph, kTimeoutTmaFull);
+      Q2B_R_ADD(3, _m1 - _m0)
+      Q2B_R_ADD(4, clock64() - _m1)
+      Q2B_R_ADD(6, 1)
       if (!ok) break;
       tc_fence_after();
       if (lane == 0) {
@@ -339,6 +368,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       }
       __syncwarp();
     }
+    Q2B_R_ADD(5, clock64() - _ml)
     if (lane == 0) {
       tc_commit(drain);
       mbar_wait(drain, 0, kTimeoutProducer);
@@ -361,12 +391,15 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     const int64_t n_kblk = out_cols >> 4, n_kt = n_kblk >> 2;
     constexpr int kChunk = Cfg::kChunkCols, kNChunks = 128 / kChunk, kG = kChunk / 16;
     float run_max = 0.f;
+    Q2B_R_T(_el)
     for (int it = grp;; it += Cfg::kEpiGroups) {
       const int64_t t = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
       if (t >= ntiles) break;
       const int buf = grp;
       const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
+      Q2B_R_T(_w0)
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
+      Q2B_R_ADD(7, clock64() - _w0)
       tc_fence_after();
       const int64_t tm = t / tiles_n, tn = t % tiles_n;
       const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
@@ -379,7 +412,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         uint32_t r[kChunk / 32][32];
 #pragma unroll
         for (int h = 0; h < kChunk / 32; ++h) tmem_ld_32x32b_x32(taddr + 32 * h, r[h]);
+        Q2B_R_T(_l1)
         tmem_ld_wait();
+        Q2B_R_ADD(8, clock64() - _l1)
         if (ch == kNChunks - 1) {
           tc_fence_before();
           __syncwarp();
@@ -406,11 +441,19 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           *reinterpret_cast<uint32_t*>(scratch + so) = fs[0] | (fs[1] << 16);
       }
     }
+    Q2B_R_ADD(10, clock64() - _el)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) run_max = fmaxf(run_max, __shfl_xor_sync(0xffffffffu, run_max, o));
     if (lane == 0) atomicMax(maxp, __float_as_uint(run_max));
   }
 
+#ifdef Q2B_RHT_STATS
+  // roles' lane 0: producer warp 0, the MMA warp, epilogue warp 0
+  if (blockIdx.x == 0 && lane == 0 && (warp == 0 || warp == Cfg::kMmaWarp || warp == Cfg::kEpiWarp0))
+    for (int i = 0; i < 12; ++i)
+      if (q2b_rs[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&g_rht_stats[i]),
+                                    static_cast<unsigned long long>(q2b_rs[i]));
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == Cfg::kMmaWarp) {
