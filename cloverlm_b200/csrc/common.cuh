@@ -529,6 +529,13 @@ __device__ __forceinline__ void tmem_cp_32x128b_x4_if(bool issue, uint32_t taddr
       : "memory");
 }
 
+// Three-input maximum (sm_100): NaN inputs are ignored as by fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Bounded wait by a whole warp; the result is the same in every lane (false if
 // any lane's wait gave up), so the warp's control flow stays converged.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned code) {

@@ -115,13 +115,13 @@ __device__ __forceinline__ void build_rotation(uint8_t* hs, const uint16_t* h, i
 // the bf16-rounded fixed scale as fp32.
 __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, uint32_t& w0, uint32_t& w1,
                                         uint32_t& fixed_bf16) {
-  // abs-max as a depth-4 tree (max is order-independent)
-  float m[8];
+  // abs-max with three-input maxima (max is exact and order-independent)
+  float v[16];
 #pragma unroll
-  for (int t = 0; t < 8; ++t) m[t] = fmaxf(fabsf(__uint_as_float(r[2 * t])), fabsf(__uint_as_float(r[2 * t + 1])));
-#pragma unroll
-  for (int t = 0; t < 4; ++t) m[t] = fmaxf(m[t], m[t + 4]);
-  const float amax = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
+  for (int t = 0; t < 16; ++t) v[t] = fabsf(__uint_as_float(r[t]));
+  const float a0 = fmax3(v[0], v[1], v[2]), a1 = fmax3(v[3], v[4], v[5]), a2 = fmax3(v[6], v[7], v[8]);
+  const float a3 = fmax3(v[9], v[10], v[11]), a4 = fmax3(v[12], v[13], v[14]);
+  const float amax = fmaxf(fmax3(a0, a1, a2), fmax3(a3, a4, v[15]));
   const float scale = amax * inv_fp4_max;
   float m3 = __uint_as_float(__float_as_uint(scale) & 0xFFF80000u);
   float f;
