@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
     const bool valid = g < ngroups;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
-    float xs[16], xa[16], m[8];
+    float xs[16], xa[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       xs[2 * k] = bf16lo(w[k]);
@@ -114,11 +114,10 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
       const uint32_t a = w[k] & 0x7FFF7FFFu;
       xa[2 * k] = bf16lo(a);
       xa[2 * k + 1] = bf16hi(a);
-      m[k] = fmaxf(xa[2 * k], xa[2 * k + 1]);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) m[k] = fmaxf(m[k], m[k + 4]);
-    const float gabs = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
+    // group abs-max with three-input maxima (exact, order-independent)
+    const float gabs = fmaxf(fmax3(fmax3(xa[0], xa[1], xa[2]), fmax3(xa[3], xa[4], xa[5]), fmax3(xa[6], xa[7], xa[8])),
+                             fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
     uint2 c;
     uint32_t s;
     const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, s);
@@ -204,7 +203,7 @@ __global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
     const bool valid = g < ngroups;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
-    float xs[16], xa[16], mm[8];
+    float xs[16], xa[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       xs[2 * k] = bf16lo(w[k]);
@@ -212,11 +211,10 @@ __global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
       const uint32_t a = w[k] & 0x7FFF7FFFu;
       xa[2 * k] = bf16lo(a);
       xa[2 * k + 1] = bf16hi(a);
-      mm[k] = fmaxf(xa[2 * k], xa[2 * k + 1]);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) mm[k] = fmaxf(mm[k], mm[k + 4]);
-    const float gabs = fmaxf(fmaxf(mm[0], mm[2]), fmaxf(mm[1], mm[3]));
+    // group abs-max with three-input maxima (exact, order-independent)
+    const float gabs = fmaxf(fmax3(fmax3(xa[0], xa[1], xa[2]), fmax3(xa[3], xa[4], xa[5]), fmax3(xa[6], xa[7], xa[8])),
+                             fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
     uint2 c;
     uint32_t sc;
     const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, sc);
