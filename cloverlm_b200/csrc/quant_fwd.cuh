@@ -42,16 +42,16 @@ __device__ __forceinline__ void fill_quant_tables(QuantTables& t, float ts) {
 // v2: one thread per 16-element group (a 32-byte load), so the group's
 // abs-max and squared errors need no shuffles; row/column of the group come
 // from a 64-bit multiply-high by a precomputed reciprocal instead of a
-// division.  Errors are accumulated on magnitudes: d = |x| - |q| * descale
-// is, bit for bit, the negation of x - q * descale whenever x < 0 (q has the
-// sign of x and rounding is symmetric), so d*d is unchanged.
+// division.  Errors are accumulated on signed values: x - q * descale is, bit
+// for bit, +-(|x| - |q| * descale) (q has the sign of x or is zero, and
+// rounding is symmetric), so d*d equals the magnitude form the reference uses.
 __device__ __forceinline__ void ldg256(const void* p, uint32_t (&r)[8]) {
   asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "l"(p));
 }
 
-__device__ __forceinline__ float quant16(const float (&xs)[16], const float (&xa)[16], float gabs, float inv_c,
+__device__ __forceinline__ float quant16(const float (&xs)[16], float gabs, float inv_c,
                                          float inv_ts, const QuantTables& tab, uint2& codes, uint32_t& s8) {
   s8 = cvt_e4m3(gabs * inv_c * inv_ts);
   const float f = tab.factor[s8];
@@ -64,14 +64,17 @@ __device__ __forceinline__ float quant16(const float (&xs)[16], const float (&xa
   }
   codes.x = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
   codes.y = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
+  // signed errors: a code carries its input's sign (or is zero), so x - q*s is
+  // exactly +-(|x| - |q|*s) (a fused multiply-add of negated inputs is the
+  // negated exact result) and its square is the magnitude form's, bit for bit
   float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float2 q0 = f16x2_to_f32x2(h[k] & 0x7FFF7FFFu);
-    const float2 d0 = ffma2(q0, make_float2(nd, nd), make_float2(xa[2 * k], xa[2 * k + 1]));
+    const float2 q0 = f16x2_to_f32x2(h[k]);
+    const float2 d0 = ffma2(q0, make_float2(nd, nd), make_float2(xs[2 * k], xs[2 * k + 1]));
     s0 = ffma2(d0, d0, s0);
-    const float2 q1 = f16x2_to_f32x2(h[4 + k] & 0x7FFF7FFFu);
-    const float2 d1 = ffma2(q1, make_float2(nd, nd), make_float2(xa[8 + 2 * k], xa[8 + 2 * k + 1]));
+    const float2 q1 = f16x2_to_f32x2(h[4 + k]);
+    const float2 d1 = ffma2(q1, make_float2(nd, nd), make_float2(xs[8 + 2 * k], xs[8 + 2 * k + 1]));
     s1 = ffma2(d1, d1, s1);
   }
   return (s0.x + s0.y) + (s1.x + s1.y);
@@ -120,11 +123,11 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
                              fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
     uint2 c;
     uint32_t s;
-    const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, s);
+    const float e6 = quant16(xs, gabs, inv6, inv_ts, tab, c, s);
     if constexpr (kFourSix) {
       uint2 c4;
       uint32_t s4;
-      const float e4 = quant16(xs, xa, gabs, inv4, inv_ts, tab, c4, s4);
+      const float e4 = quant16(xs, gabs, inv4, inv_ts, tab, c4, s4);
       if (e4 < e6) { c = c4; s = s4; }
     }
     if (valid) __stcs(codes + g, c);
@@ -217,11 +220,11 @@ __global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
                              fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
     uint2 c;
     uint32_t sc;
-    const float e6 = quant16(xs, xa, gabs, inv6, inv_ts, tab, c, sc);
+    const float e6 = quant16(xs, gabs, inv6, inv_ts, tab, c, sc);
     if constexpr (kFourSix) {
       uint2 c4;
       uint32_t s4;
-      const float e4 = quant16(xs, xa, gabs, inv4, inv_ts, tab, c4, s4);
+      const float e4 = quant16(xs, gabs, inv4, inv_ts, tab, c4, s4);
       if (e4 < e6) { c = c4; sc = s4; }
     }
     if (valid) codes[g] = c;
