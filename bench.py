@@ -43,7 +43,7 @@ KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2
 
 # Average DRAM bytes (read + write) per gemm_nvfp4_2sm_kernel launch over one step of this workload,
 # from the ncu launch list summarised in profiles/step_launches_4b_linear_set.txt.
-GEMM_DRAM_BYTES_PER_LAUNCH = 1692.7e6
+GEMM_DRAM_BYTES_PER_LAUNCH = 1671.3e6
 
 
 def flops_per_token() -> float:
