@@ -365,17 +365,17 @@ namespace q2b {
 // fit.  Scale factors: each CTA holds the A scales of its rows and the B
 // scales of all 256 columns (four-way lane-replicated, as tcgen05.cp 32x128b
 // .warpx4 writes them); one 2-CTA copy instruction fills both CTAs' TMEM.
-//   leader (rank 0): TMA warp, MMA warp, one scale-copy warp per ring slot,
+//   leader (rank 0): TMA warp, MMA warp, two groups of three scale-copy warps,
 //                    epilogue; its full[] barriers count the bytes of BOTH
 //                    CTAs (.cta_group::2 TMA completes on the leader's
 //                    barrier), its tempty[] collects both CTAs' epilogue warps.
 //   peer   (rank 1): TMA warp and epilogue.
-// tcgen05 issue blocks the issuing thread while the tensor pipe is busy, and
-// copies issued from separate warps proceed concurrently with each other and
-// with the MMAs; one thread issuing all twelve copies of a K block would
-// stall the MMA stream (measured: 2 copy warps 1.0k cycles per K block, 5-6
-// warps 0.6-0.7k, MMAs alone 0.51k).  Hence a copy warp per ring slot, each
-// committing once per K block.
+// A warp issues tcgen05.cp at ~76 cycles each and copies cost tensor-pipe
+// time once MMAs depend on them, so a K block's twelve copies are split over
+// three warps (A scales, B scales of columns 0-127, of 128-255), and two such
+// groups take alternate K blocks.  Issue loops run on converged warps with one
+// lane issuing through a predicate.  The epilogue writes D with TMA stores from
+// a per-warp staging buffer and hands TMEM back with a relaxed arrive.
 // Every wait is bounded; both CTAs meet at a cluster barrier before TMEM is
 // freed and before exit, so no CTA leaves while its peer can still touch its
 // shared memory or TMEM.
@@ -438,8 +438,9 @@ __device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
 // Warp roles (both CTAs unless noted):
 //   0  TMA producer; its loads complete on the LEADER's full[s]
 //   1  MMA issuer (leader): waits sfready[s], cta_group::2 MMAs, multicast-commits empty[s]
-//   2..kEpiWarp0-1  scale-copy issuers (leader): warp 2+s waits full[s], issues the stage's
-//      cta_group::2 tcgen05.cp into TMEM set s, commits sfready[s]
+//   2..kEpiWarp0-1  scale-copy issuers (leader): every warp waits full[s] of each stage in
+//      order; on its group's K blocks it issues its third of the stage's cta_group::2
+//      tcgen05.cp into TMEM set s and commits sfready[s] (three arrivals complete it)
 //   kEpiWarp0+  epilogue: drains its own TMEM rows, arrives on the leader's tempty
 __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
