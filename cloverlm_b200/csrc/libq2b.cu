@@ -163,6 +163,9 @@ template <int kIn, int kOut>
 int launch_rht(const CUtensorMap& tmap, const q2b::RhtParams& p, int sms, cudaStream_t st) {
   using Cfg = q2b::RhtCfg<kIn, kOut>;
   const int64_t ntiles = (p.M / 128) * (p.N / 128);
+  if (ntiles >= (int64_t(1) << 31))
+    return fail(Q2B_ERR_INVALID, "rht128: %lld x %lld is too large (more than 2^31 tiles of 128 x 128)",
+                static_cast<long long>(p.M), static_cast<long long>(p.N));
   const int grid = static_cast<int>(ntiles < sms ? ntiles : sms);
   q2b::rht_eden_kernel<kIn, kOut><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tmap, p);
   Q2B_CUDA(cudaGetLastError());

@@ -154,7 +154,7 @@ __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, ui
 // Instrumented builds only: cycle counts of CTA 0 of the last launch's roles (0 producer warp 0:
 // waiting for a free stage, 1: converting, 2: loop total; 3 MMA: waiting for a TMEM buffer,
 // 4: waiting for a stage, 5: loop total, 6: tiles; 7 epilogue warp 0: waiting for its tile,
-// 8: TMEM loads, 9: EDEN and stores, 10: loop total).  Counted in registers, added at exit.
+// 8: TMEM loads, 9 producer warp 0: waiting for its prefetched codes, 10: epilogue loop total).  Counted in registers, added at exit.
 __device__ long long g_rht_stats[12];
 #define Q2B_R_T(v) const long long v = clock64();
 #define Q2B_R_ADD(i, val) q2b_rs[i] += (val);
@@ -179,8 +179,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tiles_n = p.N >> 7;
-  const int64_t ntiles = (p.M >> 7) * tiles_n;
+  // tile indices stay below 2^31 (the launcher checks), so the per-tile
+  // row/column split is a 32-bit division, not a 64-bit software one
+  const uint32_t tiles_n = static_cast<uint32_t>(p.N >> 7);
+  const int64_t ntiles = (p.M >> 7) * static_cast<int64_t>(tiles_n);
 #ifdef Q2B_RHT_STATS
   long long q2b_rs[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
 #endif
@@ -219,7 +221,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           const int slot = it % kRhtStages;
           const uint32_t ph = (it / kRhtStages) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
-          const int tm = static_cast<int>(t / tiles_n), tn = static_cast<int>(t % tiles_n);
+          const uint32_t t32 = static_cast<uint32_t>(t);
+          const int tm = static_cast<int>(t32 / tiles_n), tn = static_cast<int>(t32 % tiles_n);
           uint8_t* dst = tiles + slot * kTileBytes;
           mbar_arrive_expect_tx(&full[slot], kTileBytes);
           tma_load_2d_hint(dst, &tmap_x, &full[slot], tn * 128, tm * 128, policy);
@@ -250,7 +253,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           return;
         }
 #endif
-        const int64_t tm = t / tiles_n, tn = t % tiles_n;
+        const uint32_t t32 = static_cast<uint32_t>(t);
+        const int64_t tm = t32 / tiles_n, tn = t32 % tiles_n;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
@@ -270,6 +274,16 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
         Q2B_R_T(_p1)
         Q2B_R_ADD(0, _p1 - _p0)
+#ifdef Q2B_RHT_STATS
+        {  // time until this tile's prefetched codes are in registers
+          uint32_t dep = 0;
+#pragma unroll
+          for (int u = 0; u < kItems; ++u) dep ^= qc[u].x ^ qc[u].w ^ sc[u];
+          asm volatile("" ::"r"(dep));
+          if (dep == 0x9e3779b9u) q2b_rs[11] += 1;
+          Q2B_R_ADD(9, clock64() - _p1)
+        }
+#endif
         uint8_t* dst = tiles + slot * kTileBytes;
 #ifdef Q2B_RHT_PROBE_NO_CONVERT
         if (true) { fence_proxy_async_smem(); mbar_arrive(&full[slot]); return true; }
@@ -401,7 +415,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
       Q2B_R_ADD(7, clock64() - _w0)
       tc_fence_after();
-      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      const uint32_t t32 = static_cast<uint32_t>(t);
+      const int64_t tm = t32 / tiles_n, tn = t32 % tiles_n;
       const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
       const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
       const uint32_t taddr0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
