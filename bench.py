@@ -398,12 +398,12 @@ def fp4_mma_peak_report(dev, iters: int = 4096, reps: int = 3) -> dict:
     from cloverlm_b200 import _lib
     stream = torch.cuda.current_stream(dev)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    _lib.call("q2b_fp4_mma_peak", 256, 0, None, stream.cuda_stream)
+    _lib.call("q2b_fp4_mma_peak", 256, None, stream.cuda_stream)
     times = []
     for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        _lib.call("q2b_fp4_mma_peak", iters, 0, None, stream.cuda_stream)
+        _lib.call("q2b_fp4_mma_peak", iters, None, stream.cuda_stream)
         e1.record(stream)
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
@@ -412,52 +412,6 @@ def fp4_mma_peak_report(dev, iters: int = 4096, reps: int = 3) -> dict:
     return {"tflops": flop / (ms / 1e3) / 1e12, "ms": ms, "iters": iters, "sm_pairs": sms // 2,
             "note": "q2b_fp4_mma_peak: back-to-back cta_group::2 M256 N256 K64 block-scaled MMAs, "
                     "operands resident in shared memory"}
-
-
-PROBE_MODES = {
-    0: "MMAs alone, tight loop on one thread",
-    1: "+ 12 scale copies per K block from the MMA thread",
-    2: "+ 12 scale copies per K block from a second warp, unsynchronised",
-    3: "+ the 4 A-scale copies only, MMA thread",
-    4: "+ 12 copies of shape 128x128b, MMA thread",
-    5: "+ 6 copies of shape 128x256b, MMA thread",
-    6: "+ copies of 2 K blocks before every 8 MMAs",
-    7: "+ copies of 4 K blocks before every 16 MMAs",
-    8: "+ 32 KB bulk loads into shared memory beside the MMAs",
-    9: "modes 2 + 8",
-    10: "five-slot ring, commit per K block (one diverged lane)",
-    11: "ring, second thread releases each slot with an arrive",
-    12: "ring, second thread issues the copies and commits",
-    13: "mode 10's loop on a converged warp, one lane issuing",
-    14: "ring with converged warps, copies on one warp",
-    15: "copies issued by the converged MMA warp before its MMAs",
-    16: "mode 14 with the next block's copies queued before this block's MMAs",
-    17: "ring with the copies split over three warps",
-}
-
-
-def fp4_probe_report(dev, iters: int = 4096) -> dict:
-    """q2b_fp4_mma_peak in every mode: SM cycles per M256 N256 K64 pair MMA measured inside the
-    kernel (clock drift between boxes drops out), and the CUDA-event rate."""
-    import torch
-    from cloverlm_b200 import _lib
-    stream = torch.cuda.current_stream(dev)
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    cyc = torch.zeros(8, dtype=torch.int64, device=dev)
-    out = {}
-    for mode, what in PROBE_MODES.items():
-        _lib.call("q2b_fp4_mma_peak", 256, mode, None, stream.cuda_stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        _lib.call("q2b_fp4_mma_peak", iters, mode, _lib.ptr(cyc), stream.cuda_stream)
-        e1.record(stream)
-        e1.synchronize()
-        c = cyc.tolist()
-        ms = e0.elapsed_time(e1)
-        out[str(mode)] = {"what": what, "cycles_per_mma": round(c[0] / iters, 1),
-                          "mhz": round(c[0] / c[1] * 1e3) if c[1] else None,
-                          "tflops": round((sms // 2) * iters * 2.0 * 256 * 256 * 64 / (ms / 1e3) / 1e12)}
-    return out
 
 
 SWEEP_M = [1024, 16384, 65536]
@@ -601,18 +555,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-small-m", action="store_true", help="skip the inference-linear latency section")
     ap.add_argument("--no-quant-sweep", action="store_true", help="skip the quantizer sweep section")
-    ap.add_argument("--fp4-probe", action="store_true",
-                    help="only run the FP4 tensor-pipe probes (q2b_fp4_mma_peak modes 0-17) and print them")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.fp4_probe:
-        import torch
-        from cloverlm_b200 import _lib
-        torch.cuda.set_device(0)
-        _lib.load(build_if_missing=False)
-        print(json.dumps({"fp4_probe": fp4_probe_report(torch.device("cuda", 0))}), flush=True)
-        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -31,6 +31,8 @@ MODE_FOUR_SIX = 1
 # name -> argtypes (all return int status, except q2b_last_error / q2b_version)
 SIGNATURES = {
     "q2b_device_status": [_P],
+    "q2b_watchdog_poll": [_P, _P],
+    "q2b_watchdog_selftest": [_I64, _P],
     "q2b_abs_max": [_P, _P, _I64, _P],
     "q2b_quant_fwd": [_P, _P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_rht_eden": [_P, _P, _P, _P, _P, _P, _INT, _P, _U64, _F, _F, _I64, _I64, _INT, _P],
@@ -43,7 +45,7 @@ SIGNATURES = {
     "q2b_quant_rows_fused": [_P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_relu2_abs_max": [_P, _P, _P, _I64, _P],
     "q2b_adamw_step": [_P, _P, _P, _P, _INT, _I64, _F, _F, _F, _F, _F, _I64, _P, _P, _P],
-    "q2b_fp4_mma_peak": [_INT, _INT, _P, _P],
+    "q2b_fp4_mma_peak": [_INT, _P, _P],
 }
 
 _lib = None
@@ -110,3 +112,67 @@ def device_status() -> int:
     code = ctypes.c_uint(0)
     call("q2b_device_status", ctypes.byref(code))
     return int(code.value)
+
+
+class WatchdogTimeout(RuntimeError):
+    """A bounded wait inside a libq2b kernel gave up; outputs since then are invalid."""
+
+
+class WatchdogMonitor:
+    """Makes a watchdog trip visible on the normal training path without a sync.
+
+    ``poll()`` is called once per step (the optimizer and the data-parallel
+    exchange call it): it checks the word copied by the previous poll, if the
+    stream has passed that copy, and raises WatchdogTimeout when it is set;
+    then it queues the next asynchronous copy (q2b_watchdog_poll) into pinned
+    host memory.  A trip is therefore reported at most one step late."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.words = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self.events = [None, None]
+        self.slot = 0
+
+    def _check(self, slot: int, block: bool) -> None:
+        ev = self.events[slot]
+        if ev is None:
+            return
+        if block:
+            ev.synchronize()
+        elif not ev.query():
+            return
+        code = int(self.words[slot].item()) & 0xFFFFFFFF
+        self.events[slot] = None
+        if code:
+            raise WatchdogTimeout(f"a libq2b kernel wait timed out (watchdog code {code}); results computed since "
+                                  f"then are invalid -- clear with q2b_device_status after handling")
+
+    def poll(self) -> None:
+        other = self.slot ^ 1
+        self._check(other, block=False)
+        self._check(self.slot, block=False)
+        stream = torch.cuda.current_stream(self.device)
+        ptr_ = ctypes.c_void_p(self.words.data_ptr() + 4 * self.slot)
+        with torch.cuda.device(self.device):
+            call("q2b_watchdog_poll", ptr_, ctypes.c_void_p(stream.cuda_stream))
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        self.events[self.slot] = ev
+        self.slot = other
+
+    def check_now(self) -> None:
+        """Block until every queued poll has landed and raise if any saw a trip."""
+        self._check(0, block=True)
+        self._check(1, block=True)
+
+
+_monitors: dict = {}
+
+
+def watchdog(device: torch.device) -> WatchdogMonitor:
+    """The process-wide WatchdogMonitor of `device`."""
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    mon = _monitors.get(key)
+    if mon is None:
+        mon = _monitors[key] = WatchdogMonitor(torch.device("cuda", key))
+    return mon

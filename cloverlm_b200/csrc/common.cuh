@@ -25,6 +25,7 @@ enum WatchdogCode : unsigned {
   kTimeoutTmemFull = 3,
   kTimeoutTmemEmpty = 4,
   kTimeoutProducer = 5,
+  kTimeoutSelfTest = 6,  // q2b_watchdog_selftest: a wait nobody completes, by construction
 };
 
 // Defined once: the library is compiled as a single translation unit.
@@ -76,22 +77,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records `code`) if it did not complete within kWaitCycles, or if another
-// wait in the grid already gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+// records `code`) if it did not complete within `limit` SM cycles, or if
+// another wait in the grid already gave up.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, unsigned code, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 1023u) == 0u) {
       if (watchdog_tripped()) return false;
-      if (clock64() - start > kWaitCycles) {
+      if (clock64() - start > limit) {
         record_timeout(code);
         return false;
       }
     }
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  return mbar_wait_limit(bar, parity, code, kWaitCycles);
+}
+
+// Health check of the timeout path: one thread waits, with a short limit, on
+// a shared-memory barrier that nothing arrives on, so the wait runs out,
+// records kTimeoutSelfTest and the kernel returns.  No copy, MMA or tensor
+// memory is involved, so nothing is left in flight.
+__global__ void watchdog_selftest_kernel(long long limit_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_wait_limit(&bar, 0, kTimeoutSelfTest, limit_cycles);
+  }
+  __syncwarp();
 }
 
 // Vector fp32 reduction into global memory (performed at L2).
@@ -345,6 +364,19 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // Correctly rounded fp32 reciprocal (IEEE round to nearest).
 __device__ __forceinline__ float rcp_rn(float x) { return __frcp_rn(x); }
+
+// The hardware's approximate reciprocal (rcp.approx.ftz.f32), the instruction
+// the reference's quantizers use for every scale reciprocal
+// (quartet2/csrc/utils.cuh:412-428, round_four_six.cu:25-31,
+// had128_utils.cuh:193,210, group_transform_and_eden.cu:222).  Using the same
+// instruction at the same points makes codes and scales bit-identical to the
+// reference's at rounding ties, where an IEEE reciprocal can land one ulp
+// away and flip the rounding.
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }

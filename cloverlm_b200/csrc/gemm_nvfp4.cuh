@@ -701,48 +701,27 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
 
 
 // ---------------------------------------------------------------------------
-// FP4 tensor-core peak probe (measurement only).  Each SM pair issues `iters`
+// FP4 tensor-core ceiling (measurement only).  Each SM pair issues `iters`
 // back-to-back cta_group::2 M256 N256 K64 block-scaled MMAs
 // (2*256*256*64 FLOP each) on operands resident in shared memory: pseudo-random
 // E2M1 codes and E4M3 scales in [0.5, 1.875], so the datapath toggles as in a
 // real GEMM.  No loads and no scale copies inside the loop: the rate is the
 // tensor pipe's own ceiling on this part, the denominator the GEMM kernels'
 // roofline fraction is quoted against.
-// mode 1 adds, before every four MMAs, the twelve scale copies (tcgen05.cp
-// 32x128b.warpx4) a K block of the GEMM needs, issued by the MMA thread;
-// mode 2 issues the same copies from a second warp, concurrently with the
-// MMAs.  Both measure what the copies cost the MMA stream.
-// mode 8 adds, in both CTAs, a warp streaming iters/4 bulk copies of 32 KB
-// from global memory into a separate shared-memory region (the operand
-// traffic a GEMM's loads bring), concurrently with the MMAs; mode 9 is
-// modes 2 and 8 together.  Modes 10-12 add the GEMM's ring hand-off over
-// five slots, without loads: 10 = the MMA thread commits each K block's
-// release; 11 = a second thread waits for each release and arrives on the
-// slot's ready barrier, which the MMA thread waits on; 12 = that thread also
-// issues the K block's twelve scale copies and signals with a commit (the
-// GEMM's scale-copy hand-off).
-__device__ __align__(128) uint8_t g_peak_src[32768];
-
 struct PeakCfg {
   static constexpr uint32_t kOpBytes = 2 * 128 * 128;  // A and this CTA's half of B, K = 256
   static constexpr uint32_t kSfBytes = 2048 + 4096;
-  static constexpr uint32_t kSinkBytes = 32768;
-  static constexpr uint32_t kUsedBytes = 1024 + kOpBytes + kSfBytes + kSinkBytes + 256;
+  static constexpr uint32_t kUsedBytes = 1024 + kOpBytes + kSfBytes + 256;
   // more than half an SM's shared memory: one CTA per SM, so no two pairs share a tensor pipe
-  static constexpr uint32_t kSmemBytes = kUsedBytes > 120 * 1024 ? kUsedBytes : 120 * 1024;
-  static constexpr int kThreads = 192;
+  static constexpr uint32_t kSmemBytes = 120 * 1024;
+  static constexpr int kThreads = 64;
 };
 
-__global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int iters, int mode, long long* cycles) {
+__global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int iters, long long* cycles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sink = smem + PeakCfg::kOpBytes + PeakCfg::kSfBytes;
-  uint64_t* drain = reinterpret_cast<uint64_t*>(sink + PeakCfg::kSinkBytes);
-  uint64_t* sinkbar = drain + 1;
-  uint64_t* rfull = drain + 2;
-  uint64_t* rempty = rfull + 5;
-  uint64_t* rissued = rempty + 5;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rissued + 5);
+  uint64_t* drain = reinterpret_cast<uint64_t*>(smem + PeakCfg::kOpBytes + PeakCfg::kSfBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   const int warp = threadIdx.x >> 5;
   const uint32_t rank = cluster_ctarank();
   for (uint32_t i = threadIdx.x; i < PeakCfg::kOpBytes / 4; i += blockDim.x) {
@@ -754,13 +733,7 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
     smem[PeakCfg::kOpBytes + i] = static_cast<uint8_t>(0x30u + ((i * 7u) & 0xFu));  // 0.5 .. 1.875
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
-    mbar_init(drain, (mode == 2 || mode == 9 || mode == 12 || mode == 14 || mode == 16) ? 2 : (mode == 17 ? 4 : 1));
-    for (int k = 0; k < 5; ++k) {
-      mbar_init(&rfull[k], mode == 17 ? 3 : 1);
-      mbar_init(&rempty[k], 1);
-      mbar_init(&rissued[k], 1);
-    }
-    mbar_init(sinkbar, 1);
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
   cluster_sync();
@@ -772,114 +745,18 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t base = smem_u32(smem);
-  const uint64_t sf_d0 = smem_desc(base + PeakCfg::kOpBytes, 0, 128, kLayoutNone);
-  const uint64_t sfb_d0 = sf_d0 + (2048 >> 4);
-  // twelve copies of one K block into scale set `set`
-  auto copy_block = [&](uint32_t set) {
-    for (int j = 0; j < 4; ++j) {
-      tmem_cp_32x128b_x4_pair(set + 4 * j, sf_d0 + 32 * j);
-      tmem_cp_32x128b_x4_pair(set + 16 + 8 * j, sfb_d0 + 32 * j);
-      tmem_cp_32x128b_x4_pair(set + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
-    }
-  };
-  // copy-cost variants (timing only; the MMAs keep reading the first set):
-  // 3 = the four A-scale copies only, 4 = twelve 128x128b copies, 5 = six 128x256b copies
-  auto copy_variant = [&](uint32_t set) {
-    if (mode == 3) {
-      for (int j = 0; j < 4; ++j) tmem_cp_32x128b_x4_pair(set + 4 * j, sf_d0 + 32 * j);
-    } else if (mode == 4) {
-      for (int j = 0; j < 12; ++j)
-        asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(set + 4 * j), "l"(sf_d0 + 32 * (j & 1))
-                     : "memory");
-    } else {
-      const uint64_t d = smem_desc(base + PeakCfg::kOpBytes, 2048, 128, kLayoutNone);
-      for (int j = 0; j < 6; ++j)
-        asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(set + 8 * j), "l"(d) : "memory");
-    }
-  };
-  if (mode == 15 && rank == 0 && warp == 1) {
-    // mode 15: the MMA warp (converged) issues each K block's twelve scale
-    // copies into one of five sets, then its four MMAs (same-thread order)
+  if (rank == 0 && warp == 1) {
     const bool lead = (threadIdx.x & 31) == 0;
-    const uint32_t idesc = idesc_nvf4(256, 256);
-    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
-    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
-    const long long c0 = clock64();
-    uint64_t g0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
-    for (int kb = 0; kb < iters / 4; ++kb) {
-      const int slot = kb % 5;
-      const uint32_t rs = tmem + 256 + 48 * slot;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, rs + 4 * j, rs + 16 + 8 * j,
-                          (kb > 0 || j > 0) ? 1u : 0u);
-      tc_commit_pair_if(lead, &rempty[slot]);
-    }
-    tc_commit_pair_leader_if(lead, drain);
-    warp_wait(drain, 0, kTimeoutProducer);
-    if (lead && cycles != nullptr && blockIdx.x == 0) {
-      uint64_t g1;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
-      cycles[0] = clock64() - c0;
-      cycles[1] = static_cast<long long>(g1 - g0);
-    }
-  } else   if ((mode == 14 || mode == 16 || mode == 17) && rank == 0 && warp == 1) {
-    // mode 14: mode 12's ring (copies by a second warp, signalled by commit) with
-    // both warps converged
-    const bool lead = (threadIdx.x & 31) == 0;
-    const uint32_t idesc = idesc_nvf4(256, 256);
-    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
-    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
-    const long long c0 = clock64();
-    uint64_t g0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
-    long long w_full = 0, w_iss = 0, t_mma = 0;
-    for (int kb = 0; kb < iters / 4; ++kb) {
-      const int slot = kb % 5;
-      const long long t0 = clock64();
-      if (!warp_wait(&rfull[slot], (kb / 5) & 1, kTimeoutTmaFull)) break;
-      const long long t1 = clock64();
-      // mode 16: the next block's copies are queued before this block's MMAs
-      if (mode == 16 && kb + 1 < iters / 4 &&
-          !warp_wait(&rissued[(kb + 1) % 5], ((kb + 1) / 5) & 1, kTimeoutTmaFull))
-        break;
-      const long long t2 = clock64();
-      w_full += t1 - t0;
-      w_iss += t2 - t1;
-      tc_fence_after();
-      const uint32_t rs = tmem + 256 + 48 * slot;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, rs + 4 * j, rs + 16 + 8 * j,
-                          (kb > 0 || j > 0) ? 1u : 0u);
-      tc_commit_pair_if(lead, &rempty[slot]);
-      t_mma += clock64() - t2;
-    }
-    tc_commit_pair_leader_if(lead, drain);
-    warp_wait(drain, 0, kTimeoutProducer);
-    if (lead && cycles != nullptr && blockIdx.x == 0) {
-      uint64_t g1;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
-      cycles[0] = clock64() - c0;
-      cycles[1] = static_cast<long long>(g1 - g0);
-      cycles[2] = w_full;
-      cycles[3] = w_iss;
-      cycles[6] = t_mma;
-    }
-  } else if (mode == 13 && rank == 0 && warp == 1) {
-    // mode 13: mode 10's loop run by the whole warp, converged, one lane issuing
-    const bool lead = (threadIdx.x & 31) == 0;
+    const uint32_t base = smem_u32(smem);
+    const uint64_t sf_d0 = smem_desc(base + PeakCfg::kOpBytes, 0, 128, kLayoutNone);
+    const uint64_t sfb_d0 = sf_d0 + (2048 >> 4);
     const uint32_t set = tmem + 256;
-    if (lead) copy_block(set);
-    __syncwarp();
+    // one K block's scale sets, copied once; every MMA reads them
+    for (int j = 0; j < 4; ++j) {
+      tmem_cp_32x128b_x4_pair_if(lead, set + 4 * j, sf_d0 + 32 * j);
+      tmem_cp_32x128b_x4_pair_if(lead, set + 16 + 8 * j, sfb_d0 + 32 * j);
+      tmem_cp_32x128b_x4_pair_if(lead, set + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
+    }
     const uint32_t idesc = idesc_nvf4(256, 256);
     const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
     const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
@@ -888,150 +765,17 @@ __global__ void __launch_bounds__(PeakCfg::kThreads, 1) fp4_mma_peak_kernel(int 
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
     for (int i = 0; i < iters; ++i) {
       const int j = i & 3;
-      const int kb = i >> 2, slot = kb % 5;
-      umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j, i > 0 ? 1u : 0u);
-      if (j == 3) tc_commit_pair_if(lead, &rempty[slot]);
+      umma_nvf4_pair_if(lead, tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j,
+                        i > 0 ? 1u : 0u);
     }
-    if (lead) {
-      tc_commit_pair_leader(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
-      if (cycles != nullptr && blockIdx.x == 0) {
-        uint64_t g1;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
-        cycles[0] = clock64() - c0;
-        cycles[1] = static_cast<long long>(g1 - g0);
-      }
-    }
-    __syncwarp();
-  } else if (rank == 0 && threadIdx.x == 32) {
-    const uint32_t set = tmem + 256;
-    if (mode != 12) copy_block(set);
-    const uint32_t idesc = idesc_nvf4(256, 256);
-    const uint64_t a_d0 = smem_desc(base, 0, 1024, kLayoutSW128);
-    const uint64_t b_d0 = smem_desc(base + 128 * 128, 0, 1024, kLayoutSW128);
-    const long long c0 = clock64();
-    uint64_t g0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
-    bool ok = true;
-    if (mode == 0) {
-      for (int i = 0; i < iters; ++i) {
-        const int j = i & 3;
-        umma_nvf4_pair(tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j, i > 0 ? 1u : 0u);
-      }
-      ok = false;
-    }
-    for (int i = 0; i < iters && ok; ++i) {
-      const int j = i & 3;
-      const int kb = i >> 2, slot = kb % 5;
-      if ((mode == 11 || mode == 12) && j == 0) {
-        ok = mbar_wait(&rfull[slot], (kb / 5) & 1, kTimeoutTmaFull);
-        tc_fence_after();
-      }
-      if (mode == 12) {
-        const uint32_t rs = tmem + 256 + 48 * slot;
-        umma_nvf4_pair(tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, rs + 4 * j, rs + 16 + 8 * j, i > 0 ? 1u : 0u);
-        if (j == 3) tc_commit_pair(&rempty[slot]);
-        continue;
-      }
-      if (mode == 1 && j == 0) copy_block(tmem + 256 + 48 * ((i >> 2) & 1) + 96);
-      if (mode >= 3 && mode <= 5 && j == 0) copy_variant(tmem + 256 + 48 * ((i >> 2) & 1) + 96);
-      // 6 / 7: the copies of 2 / 4 K blocks issued together before every 8 / 16 MMAs
-      if (mode == 6 && (i & 7) == 0) { copy_block(tmem + 352); copy_block(tmem + 400); }
-      if (mode == 7 && (i & 15) == 0) { copy_block(tmem + 352); copy_block(tmem + 400); copy_block(tmem + 352); copy_block(tmem + 400); }
-      umma_nvf4_pair(tmem, a_d0 + 2 * j, b_d0 + 2 * j, idesc, set + 4 * j, set + 16 + 8 * j, i > 0 ? 1u : 0u);
-      if (mode >= 10 && j == 3) tc_commit_pair(&rempty[slot]);
-    }
-    tc_commit_pair_leader(drain);
-    mbar_wait(drain, 0, kTimeoutProducer);
-    if (cycles != nullptr && blockIdx.x == 0) {
+    tc_commit_pair_leader_if(lead, drain);
+    warp_wait(drain, 0, kTimeoutProducer);
+    if (lead && cycles != nullptr && blockIdx.x == 0) {
       uint64_t g1;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
       cycles[0] = clock64() - c0;
       cycles[1] = static_cast<long long>(g1 - g0);
     }
-  } else if ((mode == 8 || mode == 9) && threadIdx.x == 96) {
-    const long long c0 = clock64();
-    int n = 0;
-    for (; n < iters / 4; ++n) {
-      mbar_arrive_expect_tx(sinkbar, PeakCfg::kSinkBytes);
-      bulk_load(sink, g_peak_src, PeakCfg::kSinkBytes, sinkbar);
-      if (!mbar_wait(sinkbar, n & 1, kTimeoutTmaFull)) break;
-    }
-    if (cycles != nullptr && blockIdx.x == 0) {
-      cycles[2] = clock64() - c0;
-      cycles[3] = n;
-    }
-  } else if (mode == 17 && rank == 0 && warp >= 2 && warp <= 4) {
-    // mode 17: each K block's copies split over three warps (A scales, B scales
-    // of columns 0-127, of columns 128-255), each committing to the slot's barrier
-    const bool lead = (threadIdx.x & 31) == 0;
-    const int part = warp - 2;
-    long long t_issue = 0;
-    for (int kb = 0; kb < iters / 4; ++kb) {
-      const int slot = kb % 5;
-      if (!warp_wait(&rempty[slot], ((kb / 5) & 1) ^ 1, kTimeoutSmemEmpty)) break;
-      const long long t1 = clock64();
-      tc_fence_after();
-      const uint32_t rs = tmem + 256 + 48 * slot;
-      for (int j = 0; j < 4; ++j) {
-        if (part == 0) tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
-        if (part == 1) tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
-        if (part == 2) tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
-      }
-      tc_commit_pair_leader_if(lead, &rfull[slot]);
-      t_issue += clock64() - t1;
-    }
-    if (lead && part == 0 && cycles != nullptr && blockIdx.x == 0) cycles[5] = t_issue;
-    tc_commit_pair_leader_if(lead, drain);
-    warp_wait(drain, 0, kTimeoutProducer);
-  } else if ((mode == 14 || mode == 16) && rank == 0 && warp == 2) {
-    // mode 14: mode 12's copy thread as a converged warp
-    const bool lead = (threadIdx.x & 31) == 0;
-    long long w_empty = 0, t_issue = 0;
-    for (int kb = 0; kb < iters / 4; ++kb) {
-      const int slot = kb % 5;
-      const long long t0 = clock64();
-      if (!warp_wait(&rempty[slot], ((kb / 5) & 1) ^ 1, kTimeoutSmemEmpty)) break;
-      const long long t1 = clock64();
-      w_empty += t1 - t0;
-      tc_fence_after();
-      const uint32_t rs = tmem + 256 + 48 * slot;
-      for (int j = 0; j < 4; ++j) {
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 4 * j, sf_d0 + 32 * j);
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 16 + 8 * j, sfb_d0 + 32 * j);
-        tmem_cp_32x128b_x4_pair_if(lead, rs + 20 + 8 * j, sfb_d0 + 128 + 32 * j);
-      }
-      tc_commit_pair_leader_if(lead, &rfull[slot]);
-      if (lead) mbar_arrive(&rissued[slot]);
-      __syncwarp();
-      t_issue += clock64() - t1;
-    }
-    if (lead && cycles != nullptr && blockIdx.x == 0) {
-      cycles[4] = w_empty;
-      cycles[5] = t_issue;
-    }
-    tc_commit_pair_leader_if(lead, drain);
-    warp_wait(drain, 0, kTimeoutProducer);
-  } else if ((mode == 11 || mode == 12) && rank == 0 && threadIdx.x == 64) {
-    for (int kb = 0; kb < iters / 4; ++kb) {
-      const int slot = kb % 5;
-      if (!mbar_wait(&rempty[slot], ((kb / 5) & 1) ^ 1, kTimeoutSmemEmpty)) break;
-      if (mode == 11) {
-        mbar_arrive(&rfull[slot]);
-      } else {
-        tc_fence_after();
-        copy_block(tmem + 256 + 48 * slot);
-        tc_commit_pair_leader(&rfull[slot]);
-      }
-    }
-    if (mode == 12) {
-      tc_commit_pair_leader(drain);
-      mbar_wait(drain, 0, kTimeoutProducer);
-    }
-  } else if ((mode == 2 || mode == 9) && rank == 0 && threadIdx.x == 64) {
-    for (int i = 0; i < iters; i += 4) copy_block(tmem + 256 + 48 * ((i >> 2) & 1) + 96);
-    tc_commit_pair_leader(drain);
-    mbar_wait(drain, 0, kTimeoutProducer);
   }
   tc_fence_before();
   cluster_sync();

@@ -190,6 +190,23 @@ int q2b_device_status(unsigned* code) {
   return Q2B_OK;
 }
 
+int q2b_watchdog_poll(unsigned* host_word, void* stream) {
+  Q2B_REQUIRE_NONNULL(host_word);
+  Q2B_CUDA(cudaMemcpyFromSymbolAsync(host_word, q2b::g_watchdog, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,
+                                     static_cast<cudaStream_t>(stream)));
+  return Q2B_OK;
+}
+
+int q2b_watchdog_selftest(int64_t wait_cycles, void* stream) {
+  if (wait_cycles < 1024 || wait_cycles > q2b::kWaitCycles)
+    return fail(Q2B_ERR_INVALID, "watchdog_selftest: wait_cycles must be in [1024, %lld]", q2b::kWaitCycles);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  q2b::watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(wait_cycles);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
 int q2b_abs_max(float* out, const void* x, int64_t n, void* stream) {
   Q2B_REQUIRE_PTR(x);
   Q2B_REQUIRE_NONNULL(out);
@@ -411,15 +428,36 @@ int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scra
 namespace {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[Q2B_NOALLOC_SCRATCH_BYTES + 256];
 void* g_noalloc_addr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+
+// The device address of g_noalloc_scratch on device `dev`, looked up with
+// cudaGetSymbolAddress while that device is current and cached together with
+// the current context: if the context changes (cudaDeviceReset, or a context
+// torn down and created again reloads the module), the address is looked up
+// again instead of reusing a stale one.
 int noalloc_scratch(int dev, unsigned char** out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_ctx_get_current == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    Q2B_CUDA(cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q));
+    if (fn == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(Q2B_ERR_CUDA, "cuCtxGetCurrent is not available from the driver");
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return fail(Q2B_ERR_CUDA, "no current CUDA context for the static scratch lookup");
+  if (g_noalloc_addr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     Q2B_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     if (p == nullptr) return fail(Q2B_ERR_CUDA, "cudaGetSymbolAddress returned a null scratch address");
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = static_cast<unsigned char*>(g_noalloc_addr[dev]);
   return Q2B_OK;
@@ -689,9 +727,8 @@ int q2b_gemm_nvfp4_ex(void* D, const void* A, const void* B, const void* sfa, co
   return gemm_launch(D, A, B, sfa, sfb, alpha, alpha_b, M, N, K, workspace, workspace_bytes, stream);
 }
 
-int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
+int q2b_fp4_mma_peak(int iters, long long* cycles, void* stream) {
   if (iters <= 0 || iters % 4 != 0 || iters > (1 << 24)) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: iters must be a positive multiple of 4 up to 2^24");
-  if (mode < 0 || mode > 17) return fail(Q2B_ERR_INVALID, "fp4_mma_peak: mode must be 0 .. 17");
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaLaunchConfig_t cfg = {};
@@ -706,7 +743,7 @@ int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream) {
   cfg.stream = static_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters, mode, cycles));
+  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::fp4_mma_peak_kernel, iters, cycles));
   return Q2B_OK;
 }
 

@@ -5,7 +5,7 @@
 // Quartet weight to cache max|w| for the next forward
 // (quartet2/python/quartet2/linear.py:259-270, register_optimizer_hook).
 // Here one pass does both: it updates the fp32 weight and moments and
-// reduces max|w_new| (the value the hook computes), optionally writing the
+// reduces max|bf16(w_new)| (the value the hook computes), optionally writing the
 // bf16 copy of the new weight that the forward quantizes.
 //
 // Update (AdamW with decoupled weight decay, in the operation order of
@@ -34,11 +34,14 @@ __device__ __forceinline__ float adamw_one(float& w, float& m, float& v, float g
   v = a.beta2 * v + a.one_minus_beta2 * g * g;
   const float denom = sqrtf(v) / a.bc2_sqrt + a.eps;
   w -= a.step_size * m / denom;
-  return fabsf(w);
+  // |bf16(w)|: the forward quantizes the bf16 copy of the weight, and the
+  // reference's hook takes the abs-max of that copy (bf16 rounding is
+  // monotone, so this equals bf16(max |w|))
+  return fabsf(__bfloat162float(__float2bfloat16_rn(w)));
 }
 
 // grad is fp32 (kGradBf16 = false) or bf16.  wb (optional) receives bf16(w).
-// amax (optional) accumulates the fp32 bits of max|w| with atomicMax; the
+// amax (optional) accumulates the fp32 bits of max|bf16(w)| with atomicMax; the
 // caller zeroes it first.  Vector path for 16-byte aligned tensors (four
 // elements per thread per iteration), scalar path otherwise.
 template <bool kGradBf16>

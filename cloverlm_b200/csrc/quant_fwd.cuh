@@ -6,7 +6,8 @@
 // s8 = e4m3(absmax * (so / v) / ts) for candidate v in {6, 4} (RNE: {6}),
 // codes = e2m1_rn(x / (s8' * ts)) with s8' = (s8 == 0 ? 1 : s8), and the
 // candidate with the strictly lower squared error is kept (a tie keeps 6).
-// Reciprocals are IEEE-rounded (the reference uses rcp.approx).
+// Reciprocals use rcp.approx.ftz at the same points as the reference, so
+// codes and scales match its kernels bit for bit, rounding ties included.
 //
 // Work decomposition: one thread per 16-element group (one 32-byte load), a
 // warp covers 512 consecutive elements, so its loads and 8-byte code stores
@@ -33,7 +34,7 @@ __device__ __forceinline__ void fill_quant_tables(QuantTables& t, float ts) {
   for (int i = threadIdx.x; i < 128; i += blockDim.x) {
     float s = e4m3_to_f32(static_cast<uint32_t>(i));
     float s_round = (s == 0.f) ? 1.f : s;
-    t.factor[i] = rcp_rn(s_round * ts);
+    t.factor[i] = rcp_approx_ftz(s_round * ts);
     t.descale[i] = s * ts;
   }
 }
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
   fill_quant_tables(tab, ts);
   __syncthreads();
 
-  const float inv_ts = rcp_rn(ts);
+  const float inv_ts = rcp_approx_ftz(ts);
   const float inv6 = (1.f / 6.f) * scale_override;
   const float inv4 = (1.f / 4.f) * scale_override;
   const int lane = threadIdx.x & 31;
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
   if (rank == 0 && threadIdx.x == 0) *ts_out = ts;
   fill_quant_tables(tab, ts);
   __syncthreads();
-  const float inv_ts = rcp_rn(ts);
+  const float inv_ts = rcp_approx_ftz(ts);
   const float inv6 = (1.f / 6.f) * scale_override;
   const float inv4 = (1.f / 4.f) * scale_override;
   const uint32_t n_kt = gpr >> 2;

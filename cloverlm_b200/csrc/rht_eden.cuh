@@ -125,7 +125,7 @@ __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, ui
   const float scale = amax * inv_fp4_max;
   float m3 = __uint_as_float(__float_as_uint(scale) & 0xFFF80000u);
   float f;
-  if (fabsf(m3) < FLT_MIN) { m3 = 0.f; f = 0.f; } else { f = rcp_rn(m3); }
+  if (fabsf(m3) < FLT_MIN) { m3 = 0.f; f = 0.f; } else { f = rcp_approx_ftz(m3); }
   float2 xx = make_float2(0.f, 0.f), xy = make_float2(0.f, 0.f);
   uint32_t b[8];
 #pragma unroll
@@ -141,7 +141,7 @@ __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, ui
   c[0] = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
   c[1] = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
   const float xx_t = xx.x + xx.y, xy_t = xy.x + xy.y;
-  const float corr = (xy_t == 0.f) ? 1.f : xx_t * rcp_rn(xy_t);
+  const float corr = (xy_t == 0.f) ? 1.f : xx_t * rcp_approx_ftz(xy_t);
   const float fixed = m3 * corr;
   w0 = c[0];
   w1 = c[1];
@@ -247,12 +247,6 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       uint4 qa[kItems], qb[kItems];
       uint32_t sa[kItems], sbb[kItems];
       auto load_tile = [&](int64_t t, uint4 (&q)[kItems], uint32_t (&sb)[kItems]) {
-#ifdef Q2B_RHT_PROBE_NO_LOAD
-        if (t >= 0) {
-          for (int u = 0; u < kItems; ++u) { q[u] = make_uint4(pt * 0x01010101u, t, pt, t); sb[u] = 0x3838; }
-          return;
-        }
-#endif
         const uint32_t t32 = static_cast<uint32_t>(t);
         const int64_t tm = t32 / tiles_n, tn = t32 % tiles_n;
 #pragma unroll
@@ -285,9 +279,6 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         }
 #endif
         uint8_t* dst = tiles + slot * kTileBytes;
-#ifdef Q2B_RHT_PROBE_NO_CONVERT
-        if (true) { fence_proxy_async_smem(); mbar_arrive(&full[slot]); return true; }
-#endif
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
           const int item = pt + u * 32 * Cfg::kProdWarps;
@@ -436,14 +427,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
           if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
         }
         uint32_t cw[2 * kG], fs[kG];
-#ifdef Q2B_RHT_PROBE_NO_EPI
-        for (int g = 0; g < 2 * kG; ++g) cw[g] = r[0][g];
-        for (int g = 0; g < kG; ++g) fs[g] = r[0][g + 8];
-#else
 #pragma unroll
         for (int g = 0; g < kG; ++g)
           run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
-#endif
 #pragma unroll
         for (int v = 0; v < kG / 2; ++v)
           __stcs(reinterpret_cast<uint4*>(crow + 16 * v), make_uint4(cw[4 * v], cw[4 * v + 1], cw[4 * v + 2], cw[4 * v + 3]));
@@ -513,7 +499,7 @@ __global__ void __launch_bounds__(256) sr_scales_kernel(uint2* __restrict__ sf, 
                                                         uint64_t seed, int64_t n8) {
   float gs = __uint_as_float(*max_bits) * inv_fp8_max;
   float f;
-  if (fabsf(gs) < FLT_MIN) { gs = 0.f; f = 0.f; } else { f = rcp_rn(gs); }
+  if (fabsf(gs) < FLT_MIN) { gs = 0.f; f = 0.f; } else { f = rcp_approx_ftz(gs); }
   if (blockIdx.x == 0 && threadIdx.x == 0) *ts_out = gs;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {

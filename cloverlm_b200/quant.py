@@ -256,7 +256,8 @@ def rht128_quant_eden(*, out: torch.Tensor = None, group_scales: torch.Tensor = 
 
 def rht128_quant_eden_dual(*, h: torch.Tensor, x: torch.Tensor, seed: torch.Tensor = None,
                            seed_t: torch.Tensor = None, scale_override: float = 1.0,
-                           scratch_amax: torch.Tensor = None, scratch_amax_t: torch.Tensor = None):
+                           scratch_amax: torch.Tensor = None, scratch_amax_t: torch.Tensor = None,
+                           scratch_scales: torch.Tensor = None, scratch_scales_t: torch.Tensor = None):
     """Both ``rht128_quant_eden(transpose=False)`` and ``(transpose=True)`` from ONE read of x.
 
     Returns (NVFP4Quant of x, NVFP4Quant of x^T).  No reference counterpart: it
@@ -274,8 +275,9 @@ def rht128_quant_eden_dual(*, h: torch.Tensor, x: torch.Tensor, seed: torch.Tens
     ot = torch.empty((N, M // 2), dtype=torch.uint8, device=dev)
     st = torch.empty((N, M // 16), dtype=torch.float8_e4m3fn, device=dev)
     tt = torch.empty((), dtype=torch.float32, device=dev)
-    sc = torch.empty((M * N // 16,), dtype=torch.bfloat16, device=dev)
-    sct = torch.empty((M * N // 16,), dtype=torch.bfloat16, device=dev)
+    sc = torch.empty((M * N // 16,), dtype=torch.bfloat16, device=dev) if scratch_scales is None else scratch_scales
+    sct = torch.empty((M * N // 16,), dtype=torch.bfloat16, device=dev) if scratch_scales_t is None \
+        else scratch_scales_t
     if scratch_amax is None:
         scratch_amax = torch.empty((), dtype=torch.uint32, device=dev)
     if scratch_amax_t is None:

@@ -45,8 +45,29 @@ const char* q2b_last_error(void);
 
 /* Reads and clears the device-side watchdog word of the current device: 0 if
  * no kernel wait ever timed out, else the code of the first wait that gave up.
- * Synchronizes the device. */
+ * Synchronizes the device.
+ * A trip stays set until this call clears it, and while it is set every
+ * libq2b kernel leaves at its first wait that is not already satisfied, so
+ * outputs written after a trip are invalid.  Codes: 1 TMA data not arrived,
+ * 2 shared-memory stage not released, 3 accumulator not ready, 4 accumulator
+ * not drained, 5 producer/drain wait, 6 q2b_watchdog_selftest.
+ * No counterpart in the reference (its kernels spin without a bound). */
 int q2b_device_status(unsigned* code);
+
+/* Copies the watchdog word of the current device to *host_word (pinned host
+ * memory) asynchronously on `stream`, without clearing it and without
+ * synchronizing: a training loop polls it once per step and checks the value
+ * when the stream has passed the copy.
+ * No counterpart in the reference. */
+int q2b_watchdog_poll(unsigned* host_word, void* stream);
+
+/* Exercises the timeout path: launches one thread that waits, with a limit of
+ * wait_cycles SM cycles (1024 .. 4e9), on a barrier nothing completes.  The
+ * wait gives up and records code 6 in the watchdog word (read it with
+ * q2b_device_status).  Nothing is left in flight; later launches run normally
+ * once the word is cleared.
+ * No counterpart in the reference. */
+int q2b_watchdog_selftest(int64_t wait_cycles, void* stream);
 
 /* out[0] = max |x| over n bf16 values (fp32).
  * Replaces: abs_max (torch.compile reduction), quartet2/python/quartet2/linear.py:146-148. */
@@ -113,7 +134,8 @@ int q2b_rht_eden(void* codes, void* sf, float* ts, void* scratch, unsigned* scra
  * Limit: M * N <= Q2B_NOALLOC_MAX_ELEMS (one bf16 scale per 16 elements);
  * larger inputs are rejected with Q2B_ERR_INVALID.
  * The first call on a device looks up the buffer's device address (once per
- * device, under a lock); make that first call before any stream capture.
+ * device and CUDA context, under a lock; a reset device is looked up again);
+ * make that first call before any stream capture.
  * All calls share the one buffer: calls whose kernels overlap on the GPU
  * (different streams, or different host threads, without ordering) race and
  * produce wrong results -- serialize them.  The max word is cleared on every
@@ -188,20 +210,12 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
 /* Measurement: one SM pair per two SMs issues `iters` back-to-back
  * cta_group::2 M256 N256 K64 NVFP4 block-scaled MMAs on operands resident in
  * shared memory (2*256*256*64 FLOP each; total FLOP = (SMs/2) * iters * that).
- * Time it with events on `stream` for the tensor pipe's FP4 ceiling (mode 0).
- * mode 1 adds the twelve scale-factor copies of a GEMM K block before every
- * four MMAs, from the MMA thread; mode 2 issues them from a second warp
- * (modes 3-7 vary the copy shape and batching; mode 8 streams 32 KB bulk
- * loads into shared memory beside the MMAs, mode 9 = modes 2 + 8; modes
- * 10-12 add the GEMM's five-slot ring hand-off from one diverged lane,
- * 13 is mode 10's loop on a converged warp, 14 / 16 / 17 the ring with the
- * copy warp(s) converged, 15 the copies issued by the MMA warp itself).
- * iters: a multiple of 4; mode 0 .. 17.  cycles (device, optional, 8
- * entries): SM cycles and globaltimer nanoseconds of the first pair's issue
- * loop; mode 8 adds the first CTA's load-loop cycles and load count, modes
- * 14/16 per-role wait and issue cycles.
+ * Time it with events on `stream`: the tensor pipe's FP4 ceiling, against
+ * which the GEMM's roofline fraction is quoted.  iters: a multiple of 4.
+ * cycles (device, optional, 2 entries): SM cycles and globaltimer
+ * nanoseconds of the first pair's issue loop.
  * No counterpart in the reference (its FP4 GEMM is a library call). */
-int q2b_fp4_mma_peak(int iters, int mode, long long* cycles, void* stream);
+int q2b_fp4_mma_peak(int iters, long long* cycles, void* stream);
 
 #ifdef __cplusplus
 }

@@ -3,7 +3,7 @@
 Runs IST-DASLab/CloverLM's ``src/fake_quartet.py`` (Triton kernels executed
 by the Triton interpreter on the CPU, TRITON_INTERPRET=1) on small seeded
 inputs and stores inputs and outputs under tests/golden/.  Needs the
-reference tree (default /root/reference, or $CLOVERLM_REF); the committed
+reference tree ($CLOVERLM_REF, default: a "reference" directory beside the repository); the committed
 .npz files are what the tests read, so the tests never need the reference.
 
     TRITON_INTERPRET=1 python tests/golden/make_golden.py
@@ -23,7 +23,8 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = os.environ.get("CLOVERLM_REF", "/root/reference")
+REF = os.environ.get("CLOVERLM_REF", os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(
+    os.path.abspath(__file__)))), "..", "reference"))
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 

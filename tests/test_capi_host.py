@@ -99,9 +99,9 @@ def test_adamw_rejects_bad_arguments():
 
 def test_fp4_mma_peak_rejects_bad_arguments():
     with pytest.raises(ValueError, match="multiple of 4"):
-        _lib.call("q2b_fp4_mma_peak", 6, 0, None, None)
-    with pytest.raises(ValueError, match="mode must be"):
-        _lib.call("q2b_fp4_mma_peak", 64, 18, None, None)
+        _lib.call("q2b_fp4_mma_peak", 6, None, None)
+    with pytest.raises(ValueError, match="multiple of 4"):
+        _lib.call("q2b_fp4_mma_peak", 0, None, None)
 
 
 def test_last_error_is_thread_local_text():

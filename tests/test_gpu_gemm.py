@@ -111,10 +111,10 @@ def test_fp4_mma_peak_probe_runs_in_range():
     between a plausible floor and twice the nominal dense FP4 figure."""
     dev = torch.device("cuda:0")
     stream = torch.cuda.current_stream(dev)
-    _lib.call("q2b_fp4_mma_peak", 64, 0, None, stream.cuda_stream)
+    _lib.call("q2b_fp4_mma_peak", 64, None, stream.cuda_stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    _lib.call("q2b_fp4_mma_peak", 1024, 0, None, stream.cuda_stream)
+    _lib.call("q2b_fp4_mma_peak", 1024, None, stream.cuda_stream)
     e1.record(stream)
     e1.synchronize()
     assert _lib.device_status() == 0

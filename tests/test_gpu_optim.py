@@ -57,7 +57,7 @@ def test_abs_max_and_bf16_copy_in_the_same_pass_any_alignment():
         _lib.call("q2b_adamw_step", _lib.ptr(w), _lib.ptr(m), _lib.ptr(v), _lib.ptr(grad), 0, n, 1e-2, 0.9, 0.99,
                   1e-8, 0.0, 1, _lib.ptr(wb), _lib.ptr(amax), _lib.stream_of(w))
         torch.cuda.synchronize()
-        assert amax.item() == w.abs().max().item()
+        assert amax.item() == w.to(torch.bfloat16).abs().max().item()
         assert torch.equal(wb, w.to(torch.bfloat16))
         # step 1 with zero weight decay: w - lr * g / (|g| + eps) (bias corrections cancel)
         torch.testing.assert_close(w, w_ref - 1e-2 * grad / (grad.abs() + 1e-8), rtol=1e-6, atol=1e-7)
@@ -76,8 +76,40 @@ def test_attach_replaces_the_optimizer_hook():
     opt.step()
     for layer in model:
         assert layer.weight_abs_max is not None
-        assert layer.weight_abs_max.item() == layer.weight.detach().abs().max().item()
+        # the reference hook's value: abs-max of the bf16 weight (linear.py:259-270)
+        assert layer.weight_abs_max.item() == layer.weight.detach().to(torch.bfloat16).abs().max().item()
     # the next forward uses the cached value
     with torch.autocast("cuda", dtype=torch.bfloat16):
         model(x).float().sum().backward()
+    assert _lib.device_status() == 0
+
+
+def test_register_optimizer_hook_caches_the_bf16_weight_abs_max():
+    """register_optimizer_hook (reference linear.py:259-270): after every optimizer step each
+    Quartet layer the optimizer updates holds abs_max of its bf16 weight, and the next forward
+    uses it (its output equals a forward that computes the abs-max itself)."""
+    from cloverlm_b200.linear import register_optimizer_hook
+    torch.manual_seed(1)
+    model = torch.nn.Sequential(Quartet_II_linear(256, 384, bias=False, device="cuda"),
+                                Quartet_II_linear(384, 256, bias=False, device="cuda"))
+    other = Quartet_II_linear(256, 128, bias=False, device="cuda")  # not in the optimizer: untouched
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-2)
+    handle = register_optimizer_hook(torch.nn.ModuleList([model, other]), opt)
+    x = torch.randn(1, 128, 256, device="cuda")
+    for _ in range(2):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            model(x).float().pow(2).mean().backward()
+        opt.step()
+        opt.zero_grad()
+        for layer in model:
+            want = layer.weight.detach().to(torch.bfloat16).float().abs().max()
+            assert layer.weight_abs_max.item() == want.item()
+        assert other.weight_abs_max is None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        cached = model[0](x)
+        model[0].weight_abs_max = None
+        fresh = model[0](x)
+    assert torch.equal(cached, fresh)
+    handle.remove()
+    opt.step()
     assert _lib.device_status() == 0

@@ -78,13 +78,33 @@ def test_noalloc_matches_allocating_entry_point_twice():
     assert _lib.device_status() == 0
 
 
+def test_noalloc_accepts_exactly_the_limit():
+    """M*N == Q2B_NOALLOC_MAX_ELEMS fills the whole scale area; the max word just past it
+    must stay separate (bit-identical to the allocating entry point)."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(16384, 8192, device=dev, generator=g).to(torch.bfloat16)
+    assert x.numel() == MAX_ELEMS
+    h = _h16(5, dev)
+    for transpose in (False, True):
+        got = _run(x, h, 21, transpose, noalloc=True)
+        ref = _run(x, h, 21, transpose, noalloc=False)
+        assert torch.equal(got[0], ref[0])
+        assert torch.equal(got[1], ref[1])
+        assert got[2].item() == ref[2].item()
+    assert _lib.device_status() == 0
+
+
 def test_noalloc_rejects_inputs_beyond_the_static_limit():
     dev = torch.device("cuda:0")
     x = torch.empty(128, 128, dtype=torch.bfloat16, device=dev)  # pointer only; never read
     h = _h16(0, dev)
     codes, sf, ts = _outputs(128, 128, dev)
-    rows = MAX_ELEMS // 128 + 128
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    with pytest.raises(ValueError, match="exceeds the static scratch limit"):
-        _lib.call("q2b_rht_eden_noalloc", _lib.ptr(codes), _lib.ptr(sf), _lib.ptr(ts), _lib.ptr(h), 16,
-                  _lib.ptr(x), 1, 6.0, 256.0, rows, 128, 0, st)
+    # one 128x128 tile past the limit, and far past it
+    for rows, cols in ((MAX_ELEMS // 128 + 128, 128), (MAX_ELEMS // 8192 + 2, 8192)):
+        if rows % 128:
+            rows += 128 - rows % 128
+        with pytest.raises(ValueError, match="exceeds the static scratch limit"):
+            _lib.call("q2b_rht_eden_noalloc", _lib.ptr(codes), _lib.ptr(sf), _lib.ptr(ts), _lib.ptr(h), 16,
+                      _lib.ptr(x), 1, 6.0, 256.0, rows, cols, 0, st)
