@@ -1,23 +1,25 @@
 #!/usr/bin/env python
-"""Benchmark of the Quartet-II NVFP4 linear hot path on B200.
+"""Benchmark of the Quartet-II NVFP4 training path on B200.
 
-Workload (the one its headline metric is quoted on):
-the CloverLM-4B linear set -- QKV 3584->10752, attention output 3584->3584,
-MLP up 3584->14336, MLP down 14336->3584 -- at M = 65536 tokens per GPU.
-One step = forward + backward of all four Quartet-II linears through the
-public API (Quartet_II_linear), i.e. abs-max, four-over-six quantization,
-NVFP4 GEMM, randomized-Hadamard EDEN quantization of E and E^T,
-requantization of W^T and X^T, dgrad and wgrad NVFP4 GEMMs.  On N > 1 GPUs
-each rank runs its own 65536 tokens (weak scaling) and the bf16 weight
-gradients are all-reduced (NCCL, AVG) as the data-parallel exchange step.
+Headline workload (the "train tokens/s at 1/2/4/8"
+half of its metric): one data-parallel training step of CloverLM-4B with every
+block linear a Quartet-II NVFP4 layer (cloverlm_b200.model / .train): 29
+blocks, d 3584, 28 heads x 128 with 7 KV heads, MLP 14336 (ReLU^2), vocab
+32768 tied, seq 2048, 32 sequences per GPU per step (2 micro-batches of 16,
+the first under no_sync), bf16 autocast, fused AdamW, and on N > 1 GPUs the
+bf16 gradient all-reduce (NCCL) overlapped with the last backward.  Weak
+scaling: every rank trains on its own 65536 tokens per step.  `value` is the
+whole job's tokens/s from CUDA events, max over ranks.
 
-FLOP per step per GPU = 6 * M * sum(K*N) = 60.6 TFLOP.  Inputs are synthetic
-(seeded N(0,1) activations/gradients, N(0, 0.02) weights) and larger than L2.
+At N = 1 the line also carries BASELINE config 3 (`linear_set`: fwd+bwd of the
+four 4B linear shapes at 65536 tokens, TFLOP/s -- the other half of the
+metric), config 2 (`quantizer_sweep`, GB/s), config 5 (`small_m`), the FP4
+tensor-pipe ceiling the GEMM's roofline is quoted against, and `cpu_baseline`:
+the reference's own fake-quant CPU path (src/fake_quartet.py under the Triton
+interpreter) timed on this box's host cores.
 
-`--impl reference` times the reference algorithm on the host cores instead:
-the CPU restatement in oracle/ (the reference's own implementation is CUDA
-plus a Triton emulation, neither of which runs on host cores), on a bounded
-token sample of the same four linears.
+`--impl reference` runs only that reference CPU path, one bounded sample per
+step, and reports it in the same unit.
 """
 from __future__ import annotations
 
@@ -36,18 +38,18 @@ if ROOT not in sys.path:
 
 SHAPES = [("qkv", 3584, 10752), ("attn_out", 3584, 3584), ("mlp_up", 3584, 14336), ("mlp_down", 14336, 3584)]
 METRIC = "Quartet-II linear fwd+bwd TFLOP/s at 4B shapes; train tokens/s at 1/2/4/8"
-UNIT = "TFLOP/s"
+UNIT = "tokens/s"
+# libq2b kernels each C-ABI call launches (memsets not counted)
 KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2b_rht_eden_dual": 3,
-                    "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1}
+                    "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1, "q2b_gemm_nvfp4_ex": 1, "q2b_relu2_abs_max": 1,
+                    "q2b_relu2_bwd": 1, "q2b_rope_norm_fwd": 1, "q2b_rope_norm_bwd": 1,
+                    "q2b_add_rmsnorm_amax": 1, "q2b_rmsnorm_bwd": 1, "q2b_adamw_step": 1,
+                    "q2b_watchdog_poll": 0}
 
 
-# Average DRAM bytes (read + write) per gemm_nvfp4_2sm_kernel launch over one step of this workload,
-# from the ncu launch list summarised in profiles/step_launches_4b_linear_set.txt.
-GEMM_DRAM_BYTES_PER_LAUNCH = 1671.3e6
-
-
-def flops_per_token() -> float:
-    return 6.0 * sum(k * n for _, k, n in SHAPES)
+# DRAM bytes (read + write) per NVFP4 GEMM launch of the training step, from an ncu capture
+# (profiles/); None until one is summarised.
+GEMM_TRAFFIC_PER_LAUNCH = None
 
 
 def load_peaks() -> dict:
@@ -116,93 +118,231 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# ------------------------------------------------------------ CPU (oracle)
+# ------------------------------------------------------------ instrumentation
 
-def cpu_step_tokens() -> int:
-    return int(os.environ.get("Q2B_CPU_SAMPLE_TOKENS", "128"))
+class Instrument:
+    """Bench-only accounting while `active`: libq2b kernel launches per C-ABI call, and
+    CUDA-event durations of every NVFP4 GEMM launch (the dominant kernel) on the
+    launching stream."""
+
+    def __init__(self):
+        import torch
+        from cloverlm_b200 import _lib, fusion
+        from cloverlm_b200 import linear as L
+        self.torch = torch
+        self.active = False
+        self.launches = 0
+        self.gemm = []  # (start event, end event, flop, pair kernel?)
+        self._lib, self._L, self._fusion = _lib, L, fusion
+        self._orig_call = _lib.call
+        self._orig_mm = L._fp4_mm
+        _lib.call = self._call
+        L._fp4_mm = self._mm
+        fusion._fp4_mm = self._mm
+
+    def _call(self, name, *a):
+        if self.active:
+            self.launches += KERNELS_PER_CALL.get(name, 0)
+        return self._orig_call(name, *a)
+
+    def _mm(self, a_fp4, b_fp4, a_sf, b_sf, alpha):
+        if not self.active:
+            return self._orig_mm(a_fp4, b_fp4, a_sf, b_sf, alpha)
+        torch = self.torch
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = self._orig_mm(a_fp4, b_fp4, a_sf, b_sf, alpha)
+        e.record()
+        m, n, k = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+        self.gemm.append((s, e, 2.0 * m * n * k, m % 256 == 0 and n % 256 == 0))
+        return out
+
+    def reset(self):
+        self.launches = 0
+        self.gemm = []
+
+    def gemm_summary(self, steps: int) -> dict:
+        ms = [s.elapsed_time(e) for s, e, _, _ in self.gemm]
+        flop = [f for _, _, f, _ in self.gemm]
+        pair = [p for _, _, _, p in self.gemm]
+        tot_ms, tot_f = sum(ms), sum(flop)
+        pms = sum(m for m, p in zip(ms, pair) if p)
+        pf = sum(f for f, p in zip(flop, pair) if p)
+        return {"launches_per_step": len(ms) // max(steps, 1), "ms_per_step": tot_ms / max(steps, 1),
+                "tflops": tot_f / (tot_ms / 1e3) / 1e12 if tot_ms else None,
+                "pair_kernel_share_of_flop": pf / tot_f if tot_f else None,
+                "pair_kernel_tflops": pf / (pms / 1e3) / 1e12 if pms else None}
 
 
-def run_cpu_sample(tokens: int, seed: int = 0):
-    """One fwd+bwd of the four linears on `tokens` tokens with the CPU oracle.
-    Returns (seconds, flops)."""
-    import numpy as np
+# ----------------------------------------------------- the reference's CPU path
 
-    import oracle
-    rng = np.random.default_rng(seed)
-    h16 = oracle.hadamard128_bf16()[:16].copy()
-    t_total = 0.0
-    for i, (_, K, N) in enumerate(SHAPES):
-        x = oracle.f32_to_bf16(rng.standard_normal((tokens, K), dtype=np.float32))
-        w = oracle.f32_to_bf16((0.02 * rng.standard_normal((N, K))).astype(np.float32))
-        dy = oracle.f32_to_bf16(rng.standard_normal((tokens, N), dtype=np.float32))
-        t0 = time.perf_counter()
-        oracle.linear_fwd_bwd(x, w, dy, h16, seeds=(4 * i + 1, 4 * i + 2, 4 * i + 3, 4 * i + 4))
-        t_total += time.perf_counter() - t0
-    return t_total, flops_per_token() * tokens
+def reference_cpu(tokens: int, k: int, n: int, warmup: int, steps: int, timeout: int = 900) -> dict:
+    """The reference's fake-quant Quartet-II linear (src/fake_quartet.py, Triton interpreter
+    on host cores) timed by oracle/ref_cpu.py in a subprocess."""
+    cmd = [sys.executable, os.path.join(ROOT, "oracle", "ref_cpu.py"), "--tokens", str(tokens), "--k", str(k),
+           "--n", str(n), "--warmup", str(warmup), "--steps", str(steps)]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
+    if res.returncode != 0:
+        raise RuntimeError("reference CPU path failed: " + res.stderr[-2000:])
+    return json.loads(res.stdout.strip().splitlines()[-1])
 
 
-def cpu_baseline_entry(tokens: int, reps: int = 1) -> dict:
-    import oracle
-    secs, flops = 0.0, 0.0
-    for r in range(reps):
-        s, f = run_cpu_sample(tokens, seed=r)
-        secs += s
-        flops += f
-    return {"value": flops / secs / 1e12, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"fwd+bwd of the four 4B linears on {tokens} tokens x {reps} (oracle/ C restatement, "
-                      f"{oracle.num_threads()} threads; GEMMs as fp32 numpy matmuls)"}
+def cpu_entry(r: dict, flops_per_token: float) -> dict:
+    """A timed reference CPU sample as a model-equivalent tokens/s figure."""
+    return {"value": r["flops_per_s"] / flops_per_token, "unit": UNIT, "cores": r["torch_threads"],
+            "kind": "reference",
+            "sample": (f"the reference's fake-quant Quartet-II linear (src/fake_quartet.py FakeQuartetFn, Triton "
+                       f"interpreter, fp32) fwd+bwd on X [{r['tokens']}, {r['k']}], W [{r['n']}, {r['k']}] x "
+                       f"{r['steps']}: {r['flops_per_s'] / 1e9:.3f} GFLOP/s, divided by the 4B model's "
+                       f"{flops_per_token / 1e9:.1f} GFLOP of Quartet-linear work per token (the rest of the "
+                       f"model is not counted, which favours the CPU)"),
+            "linear_gflops": r["flops_per_s"] / 1e9, "seconds": r["seconds"],
+            "cpu_model": r["cpu_model"], "os_cpu_count": r["os_cpu_count"], "torch_threads": r["torch_threads"],
+            "source": r["source"]}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import oracle
-    tokens = cpu_step_tokens()
-    for _ in range(args.warmup):
-        run_cpu_sample(tokens)
-    secs, flops = 0.0, 0.0
-    for k in range(args.steps):
-        s, f = run_cpu_sample(tokens, seed=k + 1)
-        secs += s
-        flops += f
-    value = flops / secs / 1e12
+    from cloverlm_b200.model import CloverLMConfig
+    cfg = CloverLMConfig()
+    fpt = cfg.linear_flops_per_token()
+    r = reference_cpu(args.ref_tokens, args.ref_k, args.ref_n, args.warmup, args.steps)
+    cb = cpu_entry(r, fpt)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "4B Quartet-II linear set fwd+bwd (QKV 3584->10752, O 3584->3584, "
-                               "up 3584->14336, down 14336->3584)", "tokens_per_step": tokens,
-                   "note": "bounded token sample on host cores"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-                         "sample": f"{tokens} tokens per step, oracle/ C restatement on {oracle.num_threads()} "
-                                   f"host threads"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * r["seconds"] / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 values)",
+        "data": "synthetic", "config": train_config(args, 1) | {"note": "bounded sample on host cores; each step "
+                                                                        "one fake-quant linear fwd+bwd"},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------- GPU
+# ------------------------------------------------------------ config 4: training
 
-def run_ours(args) -> None:
+def train_config(args, world: int) -> dict:
+    return {"workload": "CloverLM-4B training step (BASELINE config 4): 29 blocks, d 3584, 28 heads x 128 "
+                        "(7 KV heads), MLP 14336 ReLU^2, vocab 32768 tied, every block linear Quartet-II NVFP4",
+            "model": "CloverLM-4B", "seq_len": 2048, "micro_batch": args.micro_batch,
+            "accumulation": args.accum, "sequences_per_gpu": args.micro_batch * args.accum,
+            "global_batch": world * args.micro_batch * args.accum, "parallelism": f"dp{world}",
+            "note": "32 sequences per GPU per step reached with 2 micro-batches of 16 under no_sync "
+                    "(32 x 2048 tokens of activations do not fit beside the optimizer state in 180 GB)",
+            "l2": "inputs larger than L2 (every activation >= 235 MB)"}
+
+
+def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument) -> dict:
     import torch
     import torch.distributed as dist
 
-    import cloverlm_b200
-    from cloverlm_b200 import _lib
-    from cloverlm_b200 import linear as L
+    from cloverlm_b200.ddp import GradAllReduce
+    from cloverlm_b200.model import CloverLM, CloverLMConfig
+    from cloverlm_b200.optim import QuartetAdamW
+    from cloverlm_b200.train import TrainStep
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    cfg = CloverLMConfig()
+    torch.manual_seed(0)  # the same initial weights on every rank (what DDP's broadcast establishes)
+    model = CloverLM(cfg, device=dev)
+    opt = QuartetAdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-6, weight_decay=0.0)
+    comm = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    _lib.load(build_if_missing=False)
+        comm = GradAllReduce(list(model.parameters()), mode="overlap", bucket_mb=args.bucket_mb, copy_back=False)
+    step = TrainStep(model, opt, comm)
+    gen = torch.Generator(device=dev).manual_seed(654356 + rank * 2097593)  # per-rank data (utils_data.py:266-269)
+    shape = (args.accum, args.micro_batch, cfg.context + 1)
+    pool = [torch.randint(0, cfg.vocab_size, shape, device=dev, generator=gen) for _ in range(4)]
 
-    M = args.tokens
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    def split(ids):
+        return [(ids[i, :, :-1], ids[i, :, 1:]) for i in range(args.accum)]
+
+    losses = []
+    for i in range(args.warmup):
+        losses.append(step(split(pool[i % 4])).item())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    inst.reset()
+    inst.active = True
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        loss = step(split(pool[i % 4]))
+    ev1.record()
+    torch.cuda.synchronize()
+    inst.active = False
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    losses.append(loss.item())
+    ms = ev0.elapsed_time(ev1) / args.steps
+    gemm = inst.gemm_summary(args.steps)
+    launches = inst.launches // args.steps
+    mem = torch.cuda.max_memory_allocated(dev)
+
+    # end to end: every step's token ids copied from pinned host memory, its loss read back
+    host_ids = pool[0].cpu().pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    h2d = host_ids.numel() * host_ids.element_size()
+
+    def e2e_step():
+        ids = host_ids.to(dev, non_blocking=True)
+        out = step(split(ids))
+        loss_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    tokens = args.accum * args.micro_batch * cfg.context
+    out = {
+        "ms_per_step": ms, "tokens_per_gpu": tokens, "value": world * tokens / (ms / 1e3),
+        "e2e": {"value": world * tokens / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                "note": "TrainStep on token ids copied from pinned host memory every step, loss read back"},
+        "model_tflops": world * tokens * cfg.train_flops_per_token() / (ms / 1e3) / 1e12,
+        "linear_tflops": world * tokens * cfg.linear_flops_per_token() / (ms / 1e3) / 1e12,
+        "gemm": gemm, "gpu_launches": launches, "clocks": clocks,
+        "loss_first_last": [losses[0], losses[-1]], "max_memory_gb": mem / 1e9,
+        "params": sum(p.numel() for p in model.parameters()),
+    }
+    if comm is not None:
+        comm.close()
+    del model, opt, comm, step, pool
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
+# --------------------------------------------------------- config 3: linear set
+
+def linear_set_measure(dev, tokens: int, steps: int, warmup: int, inst: Instrument) -> dict:
+    """fwd+bwd of the four 4B linear shapes at `tokens` tokens through
+    Quartet_II_linear; TFLOP/s = 6 * M * sum(K*N) per step."""
+    import torch
+    from cloverlm_b200 import linear as L
+    M = tokens
+    g = torch.Generator(device=dev).manual_seed(1234)
     layers, xs, dys = [], [], []
     for name, K, N in SHAPES:
         lay = L.Quartet_II_linear(K, N, bias=False, device=dev, dtype=torch.bfloat16)
@@ -212,178 +352,97 @@ def run_ours(args) -> None:
         xs.append(torch.randn(M, K, device=dev, dtype=torch.bfloat16, generator=g).requires_grad_(True))
         dys.append(torch.randn(M, N, device=dev, dtype=torch.bfloat16, generator=g))
 
-    comm = None
-    if world > 1:
-        from cloverlm_b200.ddp import GradAllReduce
-        comm = GradAllReduce([lay.weight for lay in layers], mode=os.environ.get("Q2B_DDP_MODE", "overlap"))
-
-    # bench-only instrumentation: kernel launches and GEMM launch durations
-    counters = {"launches": 0, "gemm_events": [], "gemm_bytes": 0.0}
-    orig_call = _lib.call
-    state = {"timing": False}
-
-    def counting_call(name, *a):
-        if state["timing"]:
-            counters["launches"] += KERNELS_PER_CALL.get(name, 0)
-        return orig_call(name, *a)
-
-    _lib.call = counting_call
-    orig_mm = L._fp4_mm
-
-    def timed_mm(x_fp4, w_fp4, x_mx, w_mx, alpha):
-        if not state["timing"]:
-            return orig_mm(x_fp4, w_fp4, x_mx, w_mx, alpha)
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        out = orig_mm(x_fp4, w_fp4, x_mx, w_mx, alpha)
-        e.record()
-        m, n, k = x_fp4.shape[0], w_fp4.shape[0], x_fp4.shape[1] * 2
-        counters["gemm_events"].append((s, e, 2.0 * m * n * k))
-        counters["gemm_bytes"] += m * k / 2 + n * k / 2 + (m + n) * k / 16 + 2 * m * n
-        return out
-
-    L._fp4_mm = timed_mm
-
     def step():
         for lay, x, dy in zip(layers, xs, dys):
             lay.weight.grad = None
             x.grad = None
-            y = lay(x.view(1, M, -1))
-            y.backward(dy.view(1, M, -1))
-        if comm is not None:
-            comm.wait()
+            lay(x.view(1, M, -1)).backward(dy.view(1, M, -1))
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    state["timing"] = True
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    inst.reset()
+    inst.active = True
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     ev1.record()
     torch.cuda.synchronize()
-    state["timing"] = False
+    inst.active = False
+    ms = ev0.elapsed_time(ev1) / steps
+    flop = 6.0 * M * sum(k * n for _, k, n in SHAPES)
+    out = {"workload": "BASELINE config 3: QKV 3584->10752, O 3584->3584, up 3584->14336, down 14336->3584 "
+                       "(fused-QKV shapes) fwd+bwd through Quartet_II_linear",
+           "tokens": M, "ms_per_step": ms, "tflops": flop / (ms / 1e3) / 1e12, "gemm": inst.gemm_summary(steps),
+           "gpu_launches": inst.launches // steps}
+    del layers, xs, dys
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from cloverlm_b200 import _lib
+    from cloverlm_b200.model import CloverLMConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    gemm_ms = sum(s.elapsed_time(e) for s, e, _ in counters["gemm_events"])
-    gemm_flops = sum(f for _, _, f in counters["gemm_events"])
-    n_gemm = len(counters["gemm_events"])
-    gemm_alg_bytes = counters["gemm_bytes"]
-    launches = counters["launches"] // args.steps
-
-    # ---- end to end: inputs from pinned host memory, result read back, every step
-    host_x = [x.detach().cpu().pin_memory() for x in xs]
-    host_dy = [dy.cpu().pin_memory() for dy in dys]
-    h2d = sum(t.numel() * t.element_size() for t in host_x + host_dy)
-    res_host = torch.empty(len(layers), dtype=torch.float32).pin_memory()
-    d2h = res_host.numel() * res_host.element_size()
-
-    copy_stream = torch.cuda.Stream(dev)
-
-    def e2e_step():
-        # every layer's inputs go host -> device on a copy stream, issued up front, so the
-        # PCIe transfers of later layers overlap the compute of earlier ones
-        cur = torch.cuda.current_stream(dev)
-        copy_stream.wait_stream(cur)
-        staged = []
-        with torch.cuda.stream(copy_stream):
-            for hx, hdy in zip(host_x, host_dy):
-                x = hx.to(dev, non_blocking=True)
-                dy = hdy.to(dev, non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(copy_stream)
-                staged.append((x, dy, ev))
-        norms = []
-        for lay, (x, dy, ev) in zip(layers, staged):
-            cur.wait_event(ev)
-            x.record_stream(cur)
-            dy.record_stream(cur)
-            x.requires_grad_(True)
-            lay.weight.grad = None
-            y = lay(x.view(1, M, -1))
-            y.backward(dy.view(1, M, -1))
-            norms.append(lay.weight.grad.float().norm())
-        if comm is not None:
-            comm.wait()
-        res_host.copy_(torch.stack(norms), non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
-    if comm is not None:
-        comm.close()
-
-    flops_step = flops_per_token() * M
-    value = world * flops_step / (ms / 1e3) / 1e12
+        dist.init_process_group("nccl", device_id=dev)
+    _lib.load(build_if_missing=False)
+    inst = Instrument()
+    tr = train_measure(args, world, rank, local, dev, inst)
     peaks = load_peaks()
-    fp4_peak = 4.0 * peaks["bf16_tflops_sustained"]
-    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    cfg = CloverLMConfig()
+    fp4_peak = fp4_mma_peak_report(dev) if world == 1 else None
+    peak = fp4_peak["tflops"] if fp4_peak else 4.0 * peaks["bf16_tflops_sustained"]
+    achieved = tr["gemm"]["tflops"]
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e4m3 block-16, fp32 accumulate, bf16 io)",
-        "data": "synthetic (seeded N(0,1) activations and gradients, N(0,0.02) weights)",
-        "config": {"workload": "4B Quartet-II linear set fwd+bwd: QKV 3584->10752, O 3584->3584, "
-                               "up 3584->14336, down 14336->3584 (BASELINE config 3)",
-                   "tokens_per_gpu": M, "tokens_per_s": world * M / (ms / 1e3),
-                   "parallelism": f"dp{world}",
-                   "allreduce": (f"bf16 NCCL AVG ({comm.mode})" if comm is not None else None),
-                   "l2": "inputs larger than L2 (>= 470 MB per operand)"},
-        "e2e": {"value": world * flops_step / (e2e_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "Quartet_II_linear API; activations and output gradients copied from pinned host "
-                        "memory each step (on a copy stream, overlapping earlier layers' compute), "
-                        "weight-gradient norms read back"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_nvfp4_2sm_kernel", "achieved": achieved,
-                     "peak": fp4_peak, "unit": "TFLOP/s",
-                     "frac": (achieved / fp4_peak) if achieved else None,
-                     "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
-                     "algorithmic_bytes_per_launch": gemm_alg_bytes / max(n_gemm, 1),
-                     "peak_note": "dense NVFP4 = 4 x measured sustained bf16 (MEASURED_PEAKS.json "
-                                  f"{peaks['source']}); nominal dense fp4 9000 TFLOP/s",
-                     "gemm_launches_per_step": n_gemm // max(args.steps, 1),
-                     "gemm_share_of_step": (gemm_ms / args.steps) / ms},
-        "gpu_launches": launches,
-        "clocks": clocks,
+        "metric": METRIC, "value": tr["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": tr["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 linears (e2m1 x e4m3 block-16, fp32 accumulate), bf16 autocast "
+                                      "elsewhere, fp32 master weights",
+        "data": "synthetic (uniform token ids, per-rank seeds; random-init weights)",
+        "config": train_config(args, world) | {"tokens_per_gpu": tr["tokens_per_gpu"],
+                                               "allreduce": "bf16 NCCL AVG, 256 MB buckets launched during the "
+                                                            "last backward" if world > 1 else None},
+        "e2e": tr["e2e"],
+        "roofline": {"bound": "tensor", "kernel": "q2b_gemm_nvfp4 (gemm_nvfp4_2sm_kernel for the 256-aligned "
+                                                  "shapes, gemm_nvfp4_kernel otherwise) inside the training step",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if achieved else None, "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                     "peak_note": ("FP4 tensor-pipe ceiling measured in this run by q2b_fp4_mma_peak"
+                                   if fp4_peak else "4 x measured sustained bf16 (MEASURED_PEAKS.json)"),
+                     "frac_of_4x_bf16_sustained": achieved / (4.0 * peaks["bf16_tflops_sustained"]) if achieved
+                     else None,
+                     "gemm_share_of_step": tr["gemm"]["ms_per_step"] / tr["ms_per_step"]},
+        "gpu_launches": tr["gpu_launches"],
+        "clocks": tr["clocks"],
+        "train": {k: tr[k] for k in ("model_tflops", "linear_tflops", "gemm", "loss_first_last", "max_memory_gb",
+                                     "params")},
         "lib": _lib.lib_path(),
     }
-    if world == 1:
-        pk = fp4_mma_peak_report(dev)
-        line["roofline"]["fp4_mma_peak_measured"] = pk
-        if achieved:
-            line["roofline"]["frac_of_fp4_mma_peak"] = achieved / pk["tflops"]
+    if fp4_peak:
+        line["roofline"]["fp4_mma_peak_measured"] = fp4_peak
+    if world == 1 and not args.no_linear_set:
+        ls = linear_set_measure(dev, args.tokens, args.linear_steps, args.warmup, inst)
+        ls["frac_of_fp4_peak"] = ls["tflops"] / peak
+        line["linear_set"] = ls
     if world == 1 and not args.no_small_m:
         line["small_m"] = small_m_report(dev)
     if world == 1 and not args.no_quant_sweep:
         line["quantizer_sweep"] = quant_sweep_report(dev)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_entry(cpu_step_tokens())
+        try:
+            line["cpu_baseline"] = cpu_entry(reference_cpu(128, 1024, 1024, 0, 1), cfg.linear_flops_per_token())
+        except Exception as e:  # reported, not fatal: the GPU numbers stand on their own
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "error": str(e)[-300:]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -551,7 +610,16 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--micro-batch", dest="micro_batch", type=int, default=16)
+    ap.add_argument("--accum", type=int, default=2, help="micro-batches per step (the first ones under no_sync)")
+    ap.add_argument("--bucket-mb", dest="bucket_mb", type=float, default=256.0)
+    ap.add_argument("--e2e-steps", dest="e2e_steps", type=int, default=4)
+    ap.add_argument("--tokens", type=int, default=65536, help="tokens of the config-3 linear-set section")
+    ap.add_argument("--linear-steps", dest="linear_steps", type=int, default=10)
+    ap.add_argument("--ref-tokens", dest="ref_tokens", type=int, default=128)
+    ap.add_argument("--ref-k", dest="ref_k", type=int, default=512)
+    ap.add_argument("--ref-n", dest="ref_n", type=int, default=512)
+    ap.add_argument("--no-linear-set", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-small-m", action="store_true", help="skip the inference-linear latency section")
     ap.add_argument("--no-quant-sweep", action="store_true", help="skip the quantizer sweep section")

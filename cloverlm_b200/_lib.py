@@ -44,6 +44,11 @@ SIGNATURES = {
     "q2b_gemm_nvfp4_ex": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P],
     "q2b_quant_rows_fused": [_P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_relu2_abs_max": [_P, _P, _P, _I64, _P],
+    "q2b_relu2_bwd": [_P, _P, _P, _I64, _P],
+    "q2b_rope_norm_fwd": [_P, _P, _P, _P, _P, _I64, _INT, _INT, _P],
+    "q2b_rope_norm_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _INT, _INT, _P],
+    "q2b_add_rmsnorm_amax": [_P, _P, _P, _P, _P, _P, _P, _I64, _INT, _F, _P],
+    "q2b_rmsnorm_bwd": [_P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _INT, _P],
     "q2b_adamw_step": [_P, _P, _P, _P, _INT, _I64, _F, _F, _F, _F, _F, _I64, _P, _P, _P],
     "q2b_fp4_mma_peak": [_INT, _P, _P],
 }

@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -15,6 +16,7 @@
 #include "quant_fwd.cuh"
 #include "rht_eden.cuh"
 #include "optim.cuh"
+#include "glue.cuh"
 
 namespace {
 
@@ -187,6 +189,112 @@ int q2b_device_status(unsigned* code) {
   Q2B_CUDA(cudaMemcpyFromSymbol(&v, q2b::g_watchdog, sizeof(unsigned)));
   Q2B_CUDA(cudaMemcpyToSymbol(q2b::g_watchdog, &zero, sizeof(unsigned)));
   *code = v;
+  return Q2B_OK;
+}
+
+// ---------------------------------------------------------------- block glue
+int q2b_rope_norm_fwd(void* out, float* norm_out, const void* x, const float* cos_sin, const float* scale,
+                      int64_t rows, int heads, int seq, void* stream) {
+  Q2B_REQUIRE_PTR(out);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_NONNULL(norm_out);
+  Q2B_REQUIRE_NONNULL(cos_sin);
+  if (rows <= 0 || heads <= 0 || heads > 64 || seq <= 0)
+    return fail(Q2B_ERR_INVALID, "rope_norm: rows, heads (1..64) and seq must be positive");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  const int64_t nvec = rows * heads;
+  const int64_t blocks = std::min<int64_t>((nvec + 15) / 16, static_cast<int64_t>(sms) * 16);
+  q2b::rope_norm_fwd_kernel<<<static_cast<unsigned>(blocks), q2b::kRopeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(out), norm_out, static_cast<const uint4*>(x), reinterpret_cast<const float2*>(cos_sin),
+      scale, nvec, heads, seq);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_rope_norm_bwd(void* dx, float* dscale, const void* dout, const void* out, const float* norm,
+                      const float* cos_sin, const float* scale, int64_t rows, int heads, int seq, void* stream) {
+  Q2B_REQUIRE_PTR(dx);
+  Q2B_REQUIRE_PTR(dout);
+  Q2B_REQUIRE_PTR(out);
+  Q2B_REQUIRE_NONNULL(norm);
+  Q2B_REQUIRE_NONNULL(cos_sin);
+  if (rows <= 0 || heads <= 0 || heads > 64 || seq <= 0)
+    return fail(Q2B_ERR_INVALID, "rope_norm: rows, heads (1..64) and seq must be positive");
+  if ((dscale == nullptr) != (scale == nullptr))
+    return fail(Q2B_ERR_INVALID, "rope_norm_bwd: dscale and scale are given together or not at all");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  const int64_t nvec = rows * heads;
+  const int64_t blocks = std::min<int64_t>((nvec + 15) / 16, static_cast<int64_t>(sms) * 8);
+  q2b::rope_norm_bwd_kernel<<<static_cast<unsigned>(blocks), q2b::kRopeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(dx), dscale, static_cast<const uint4*>(dout), static_cast<const uint4*>(out), norm,
+      reinterpret_cast<const float2*>(cos_sin), scale, nvec, heads, seq);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_add_rmsnorm_amax(float* x_out, void* xb_out, float* rstd_out, float* amax, const float* x, const void* y,
+                         const float* w, int64_t rows, int d, float eps, void* stream) {
+  Q2B_REQUIRE_PTR(x_out);
+  Q2B_REQUIRE_PTR(xb_out);
+  Q2B_REQUIRE_PTR(x);
+  Q2B_REQUIRE_PTR(y);
+  Q2B_REQUIRE_PTR(w);
+  Q2B_REQUIRE_NONNULL(rstd_out);
+  Q2B_REQUIRE_NONNULL(amax);
+  if (rows <= 0 || d <= 0 || d % 8 != 0 || d > 8 * q2b::kNormThreads * q2b::kNormMaxVecs)
+    return fail(Q2B_ERR_INVALID, "add_rmsnorm_amax: d must be a positive multiple of 8 up to %d",
+                8 * q2b::kNormThreads * q2b::kNormMaxVecs);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Q2B_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
+  const int64_t blocks = std::min<int64_t>(rows, static_cast<int64_t>(sms) * 8);
+  q2b::add_rmsnorm_amax_kernel<<<static_cast<unsigned>(blocks), q2b::kNormThreads, 0, st>>>(
+      x_out, static_cast<uint4*>(xb_out), rstd_out, reinterpret_cast<unsigned*>(amax), x,
+      static_cast<const uint4*>(y), w, rows, d, eps);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_rmsnorm_bwd(float* dx, void* dy, float* dw_partial, int64_t partial_rows, const float* g, const void* gb,
+                    const void* y, const float* rstd, const float* w, int64_t rows, int d, void* stream) {
+  Q2B_REQUIRE_PTR(dx);
+  Q2B_REQUIRE_PTR(dy);
+  Q2B_REQUIRE_PTR(dw_partial);
+  Q2B_REQUIRE_PTR(g);
+  Q2B_REQUIRE_PTR(y);
+  Q2B_REQUIRE_PTR(w);
+  Q2B_REQUIRE_NONNULL(rstd);
+  if (gb != nullptr && !aligned16(gb)) return fail(Q2B_ERR_INVALID, "Pointer `gb` is not aligned to 16 bytes");
+  if (rows <= 0 || d <= 0 || d % 8 != 0 || d > 8 * q2b::kNormThreads * q2b::kNormMaxVecs)
+    return fail(Q2B_ERR_INVALID, "rmsnorm_bwd: d must be a positive multiple of 8 up to %d",
+                8 * q2b::kNormThreads * q2b::kNormMaxVecs);
+  if (partial_rows <= 0 || partial_rows > rows)
+    return fail(Q2B_ERR_INVALID, "rmsnorm_bwd: partial_rows must be in [1, rows]");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  q2b::rmsnorm_bwd_kernel<<<static_cast<unsigned>(partial_rows), q2b::kNormThreads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(dx, static_cast<uint4*>(dy), dw_partial, g,
+                                                                 static_cast<const uint4*>(gb),
+                                                                 static_cast<const uint4*>(y), rstd, w, rows, d);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
+int q2b_relu2_bwd(void* da, const void* a, const void* g, int64_t n, void* stream) {
+  Q2B_REQUIRE_PTR(da);
+  Q2B_REQUIRE_PTR(a);
+  Q2B_REQUIRE_PTR(g);
+  if (n <= 0 || n % 8 != 0) return fail(Q2B_ERR_INVALID, "relu2_bwd: n must be a positive multiple of 8");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  const int64_t nvec = n / 8;
+  const int64_t blocks = std::min<int64_t>((nvec + 255) / 256, static_cast<int64_t>(sms) * 8);
+  q2b::relu2_bwd_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(da), static_cast<const uint4*>(a), static_cast<const uint4*>(g), nvec);
+  Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
 }
 

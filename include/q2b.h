@@ -207,6 +207,47 @@ int q2b_adamw_step(float* w, float* exp_avg, float* exp_avg_sq, const void* grad
                    float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step, void* w_bf16,
                    float* amax, void* stream);
 
+/* ---- CloverLM block glue (the training step around the Quartet linears) ----
+ * No counterparts as single kernels in the reference: each fuses a chain of
+ * PyTorch elementwise ops of src/models/transformer.py / mlp.py into one pass.
+ *
+ * RoPE (base-1024 table, interleaved pairs) + sphere norm (eps 1e-12) +
+ * optional per-head scale of x bf16 [rows, heads, 128] (row r at position
+ * r % seq): out = scale[h] * n / max(|n|, 1e-12) with n = bf16(rope(x));
+ * norm_out [rows, heads] fp32 keeps max(|n|, 1e-12) for the backward.
+ * cos_sin: fp32 [seq, 64, 2] (cos, sin).  scale: fp32 [heads] or NULL.
+ * Replaces: apply_rope + sphere_norm + Q = scale * Q,
+ * src/models/transformer.py:63-74,357-363,177-185. */
+int q2b_rope_norm_fwd(void* out, float* norm_out, const void* x, const float* cos_sin, const float* scale,
+                      int64_t rows, int heads, int seq, void* stream);
+
+/* Gradient of q2b_rope_norm_fwd: dx bf16 [rows, heads, 128] from dout and the
+ * forward's out and norm_out; dscale[h] += sum over rows of dout * out / scale
+ * (dscale and scale both NULL when there is no scale; the caller zeroes it). */
+int q2b_rope_norm_bwd(void* dx, float* dscale, const void* dout, const void* out, const float* norm,
+                      const float* cos_sin, const float* scale, int64_t rows, int heads, int seq, void* stream);
+
+/* Residual RMSNorm with the next Quartet layer's abs-max: for rows of d
+ * (a multiple of 8, at most 4096) values, rstd = 1/sqrt(mean(y^2) + eps),
+ * x_out = x + (y * rstd) * w (fp32), xb_out = bf16(x_out), *amax =
+ * max |xb_out|, rstd_out[r] = rstd.  x, x_out, w fp32; y, xb_out bf16.
+ * Replaces: Y = out_att_norm(Y); Y__ = X + Y (and the MLP's), followed by the
+ * next Quartet_II_fn's abs_max of its input, src/models/transformer.py:380-395,
+ * quartet2/python/quartet2/linear.py:179-183. */
+int q2b_add_rmsnorm_amax(float* x_out, void* xb_out, float* rstd_out, float* amax, const float* x, const void* y,
+                         const float* w, int64_t rows, int d, float eps, void* stream);
+
+/* Gradient of q2b_add_rmsnorm_amax: with g = g (fp32) + gb (bf16, may be
+ * NULL), dx = g (fp32; dx may be g), dy = rstd * (g*w - yhat * mean(g*w*yhat))
+ * (bf16, yhat = y * rstd), and dw_partial [partial_rows, d] fp32 holds the
+ * per-block sums of g * yhat (partial_rows blocks; the caller sums them). */
+int q2b_rmsnorm_bwd(float* dx, void* dy, float* dw_partial, int64_t partial_rows, const float* g, const void* gb,
+                    const void* y, const float* rstd, const float* w, int64_t rows, int d, void* stream);
+
+/* da = bf16(2 * relu(a) * g) for n (a multiple of 8) bf16 values.
+ * Replaces: the autograd backward of relu(x)**2, src/models/mlp.py:34-38. */
+int q2b_relu2_bwd(void* da, const void* a, const void* g, int64_t n, void* stream);
+
 /* Measurement: one SM pair per two SMs issues `iters` back-to-back
  * cta_group::2 M256 N256 K64 NVFP4 block-scaled MMAs on operands resident in
  * shared memory (2*256*256*64 FLOP each; total FLOP = (SMs/2) * iters * that).

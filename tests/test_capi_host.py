@@ -25,6 +25,9 @@ def test_library_loads_and_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert set(_lib.SIGNATURES) <= set(names)
+    # every int-returning entry point has its argument types declared for ctypes
+    # (an undeclared one would pass 64-bit sizes and floats wrongly)
+    assert set(names) - {"q2b_last_error", "q2b_version", "q2b_gemm_workspace_bytes"} <= set(_lib.SIGNATURES)
     assert lib.q2b_version() >= 100
 
 

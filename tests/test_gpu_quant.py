@@ -22,8 +22,11 @@ TIE_FRACTION = 1e-4
 # The forward kernels use the reference's rcp.approx.ftz reciprocal (so they match
 # the reference's kernels bit for bit, tests/test_gpu_ref_parity.py); the oracle
 # uses IEEE reciprocals, which can differ by one ulp and flip a value that sits
-# exactly on a rounding boundary.  Everything else is identical.
-RCP_TIE_FRACTION = 1e-4
+# exactly on a rounding boundary.  Everything else is identical.  Inputs with
+# outliers make such ties common (a few 1e-4 of the bytes, measured 3.4e-4 at
+# [2048, 3584]), so the bound here is 2e-3; against the reference's own
+# kernels the forward output is bit-exact.
+RCP_TIE_FRACTION = 2e-3
 
 SHAPES = [(128, 128), (256, 128), (128, 1024), (1024, 640), (512, 3584)]
 
