@@ -41,7 +41,7 @@ METRIC = "Quartet-II linear fwd+bwd TFLOP/s at 4B shapes; train tokens/s at 1/2/
 UNIT = "tokens/s"
 # libq2b kernels each C-ABI call launches (memsets not counted)
 KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2b_rht_eden_dual": 3,
-                    "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1, "q2b_gemm_nvfp4_ex": 1, "q2b_relu2_abs_max": 1,
+                    "q2b_rht_requant": 2, "q2b_gemm_nvfp4": 1, "q2b_gemm_nvfp4_f32": 1, "q2b_gemm_nvfp4_ex": 1, "q2b_relu2_abs_max": 1,
                     "q2b_relu2_bwd": 1, "q2b_rope_norm_fwd": 1, "q2b_rope_norm_bwd": 1,
                     "q2b_add_rmsnorm_amax": 1, "q2b_rmsnorm_bwd": 1, "q2b_adamw_step": 1,
                     "q2b_watchdog_poll": 0}
@@ -136,8 +136,10 @@ class Instrument:
         self._lib, self._L, self._fusion = _lib, L, fusion
         self._orig_call = _lib.call
         self._orig_mm = L._fp4_mm
+        self._orig_mm32 = L._fp4_mm_f32
         _lib.call = self._call
         L._fp4_mm = self._mm
+        L._fp4_mm_f32 = self._mm32
         fusion._fp4_mm = self._mm
 
     def _call(self, name, *a):
@@ -146,12 +148,18 @@ class Instrument:
         return self._orig_call(name, *a)
 
     def _mm(self, a_fp4, b_fp4, a_sf, b_sf, alpha):
+        return self._timed(self._orig_mm, a_fp4, b_fp4, a_sf, b_sf, alpha)
+
+    def _mm32(self, a_fp4, b_fp4, a_sf, b_sf, alpha):
+        return self._timed(self._orig_mm32, a_fp4, b_fp4, a_sf, b_sf, alpha)
+
+    def _timed(self, fn, a_fp4, b_fp4, a_sf, b_sf, alpha):
         if not self.active:
-            return self._orig_mm(a_fp4, b_fp4, a_sf, b_sf, alpha)
+            return fn(a_fp4, b_fp4, a_sf, b_sf, alpha)
         torch = self.torch
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        out = self._orig_mm(a_fp4, b_fp4, a_sf, b_sf, alpha)
+        out = fn(a_fp4, b_fp4, a_sf, b_sf, alpha)
         e.record()
         m, n, k = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
         self.gemm.append((s, e, 2.0 * m * n * k, m % 256 == 0 and n % 256 == 0))

@@ -31,7 +31,7 @@ struct GemmParams {
   const uint8_t* sfb;   // blocked [N, K/16]
   const float* alpha;
   const float* alpha_b; // optional second factor of alpha (nullptr = 1)
-  __nv_bfloat16* D;     // [m_valid, N] row-major
+  void* D;              // [m_valid, N] row-major, bf16 (or fp32 for the kOutF32 kernels)
   int64_t m_valid;      // rows of A and D that exist (A rows past it read as zero through TMA)
   int splits;           // K split into this many ranges per output tile (1 = none)
   float* ws;            // splits > 1: fp32 partial tiles [tiles][128][BN], zero between calls
@@ -78,7 +78,7 @@ struct GemmCfg {
 // copies issued by a second warp overlap the MMAs of earlier stages.  Column
 // set s is free again when full[s] fires, because the producer reloads stage
 // s only after the MMAs that read set s have completed (empty[s]).
-template <int BN>
+template <int BN, bool kOutF32 = false>
 __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const GemmParams p) {
@@ -257,7 +257,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       const int trow = q * 32 + lane;
       const int64_t row = tm * Cfg::BM + trow;
       const bool live = row < p.m_valid;
-      __nv_bfloat16* drow = p.D + row * p.N + tn * BN + c0;
+      __nv_bfloat16* drow = static_cast<__nv_bfloat16*>(p.D) + row * p.N + tn * BN + c0;
+      float* frow = static_cast<float*>(p.D) + row * p.N + tn * BN + c0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + c0;
       constexpr int kChunks = kColsPerWarp / 32;
       if constexpr (BN == 128) {
@@ -299,13 +300,20 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                   const float4 v = __ldcg(reinterpret_cast<const float4*>(wrow + ch * 32 + 4 * k));
-                  o[2 * k] = pack_bf16x2(v.x, v.y);
-                  o[2 * k + 1] = pack_bf16x2(v.z, v.w);
+                  if constexpr (kOutF32) {
+                    reinterpret_cast<float4*>(frow + ch * 32)[k] = v;
+                  } else {
+                    o[2 * k] = pack_bf16x2(v.x, v.y);
+                    o[2 * k + 1] = pack_bf16x2(v.z, v.w);
+                  }
                   __stcg(reinterpret_cast<float4*>(wrow + ch * 32 + 4 * k), make_float4(0.f, 0.f, 0.f, 0.f));
                 }
-                uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+                if constexpr (!kOutF32) {
+                  uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                  for (int k = 0; k < 4; ++k)
+                    dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                }
               }
             }
             if (lane == 0) *ctr = 0u;
@@ -318,6 +326,29 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       // and hand the TMEM buffer back to the MMA warp at once; the global
       // stores then overlap the next tile's MMAs.
       constexpr int kHalf = kChunks > 1 ? kChunks / 2 : 1;
+      if constexpr (kOutF32) {
+        // fp32 output: each 32-column chunk goes out as soon as it is loaded
+        // (the accumulator is released after the last chunk's load)
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + ch * 32, r);
+          tmem_ld_wait();
+          if (ch == kChunks - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
+          }
+          if (live) {
+            float4* dst = reinterpret_cast<float4*>(frow + ch * 32);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              dst[k] = make_float4(__uint_as_float(r[4 * k]) * alpha, __uint_as_float(r[4 * k + 1]) * alpha,
+                                   __uint_as_float(r[4 * k + 2]) * alpha, __uint_as_float(r[4 * k + 3]) * alpha);
+          }
+        }
+        continue;
+      }
       uint32_t o[kChunks][16];
 #pragma unroll
       for (int h0 = 0; h0 < kChunks; h0 += kHalf) {
@@ -442,6 +473,7 @@ __device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
 //      order; on its group's K blocks it issues its third of the stage's cta_group::2
 //      tcgen05.cp into TMEM set s and commits sfready[s] (three arrivals complete it)
 //   kEpiWarp0+  epilogue: drains its own TMEM rows, arrives on the leader's tempty
+template <bool kOutF32 = false>
 __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
@@ -659,12 +691,20 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       // relaxed: only tensor memory changes hands, its reads already complete
       if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader);
       if (e == 0) { Q2B_S_ADD(8, _e2 - _e1) Q2B_S_ADD(9, _e3 - _e2) Q2B_S_ADD(10, _e4 - _e3) Q2B_S_ADD(11, _e5 - _e4) }
+      // one box = 32 rows x 64 bytes: 32 bf16 columns, or 16 fp32 columns
+      constexpr int kBoxCols = kOutF32 ? 16 : 32;
 #pragma unroll
-      for (int ch = 0; ch < kCols / 32; ++ch) {
+      for (int bx = 0; bx < kCols / kBoxCols; ++bx) {
         uint32_t o[16];
+        if constexpr (kOutF32) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          o[k] = pack_bf16x2(__uint_as_float(r[ch][2 * k]) * alpha, __uint_as_float(r[ch][2 * k + 1]) * alpha);
+          for (int k = 0; k < 16; ++k)
+            o[k] = __float_as_uint(__uint_as_float(r[bx >> 1][16 * (bx & 1) + k]) * alpha);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o[k] = pack_bf16x2(__uint_as_float(r[bx][2 * k]) * alpha, __uint_as_float(r[bx][2 * k + 1]) * alpha);
+        }
         // the previous box's store must have read the staging buffer
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
@@ -675,7 +715,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmap_d, stage, static_cast<int>(tn * 256 + c0 + ch * 32), row0);
+          tma_store_2d(&tmap_d, stage, static_cast<int>(tn * 256 + c0 + bx * kBoxCols), row0);
           bulk_commit_group();
         }
       }

@@ -100,9 +100,12 @@ int device_setup(int* dev_out, int* sms_out) {
     Q2B_CUDA(set_smem(rht_eden_kernel<kInBf16, kOutCols>, RhtCfg<kInBf16, kOutCols>::kSmemBytes));
     Q2B_CUDA(set_smem(rht_eden_kernel<kInBf16, kOutBoth>, RhtCfg<kInBf16, kOutBoth>::kSmemBytes));
     Q2B_CUDA(set_smem(rht_eden_kernel<kInFp4, kOutCols>, RhtCfg<kInFp4, kOutCols>::kSmemBytes));
-    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256>, GemmCfg<256>::kSmemBytes));
-    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128>, GemmCfg<128>::kSmemBytes));
-    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256, false>, GemmCfg<256>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128, false>, GemmCfg<128>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256, true>, GemmCfg<256>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128, true>, GemmCfg<128>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<false>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<true>, Gemm2Cfg::kSmemBytes));
     Q2B_CUDA(set_smem(fp4_mma_peak_kernel, PeakCfg::kSmemBytes));
     d.ready = true;
   }
@@ -730,21 +733,23 @@ int64_t split_ws_bytes(const SplitPlan& sp) {
 
 int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                 const float* alpha_b, int64_t m_valid, int64_t N, int64_t K, void* ws, int64_t ws_bytes,
-                void* stream) {
+                void* stream, bool out_f32 = false) {
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t M = (m_valid + 127) / 128 * 128;
   CUtensorMap ta, tb;
   q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha, alpha_b,
-                    static_cast<__nv_bfloat16*>(D), m_valid, 1, nullptr, nullptr};
+                    D, m_valid, 1, nullptr, nullptr};
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
   if (m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms &&
       (reinterpret_cast<uintptr_t>(D) & 15u) == 0) {
     // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair; D written by TMA stores
     CUtensorMap tsa, tsb, td;
-    if (int r = make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    // store boxes of 32 rows x 64 bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle
+    if (int r = out_f32 ? make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                        : make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return r;
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
     if (int r = make_tmap(&tsa, sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, M * K / 16 / 256, 256, 8,
@@ -767,7 +772,10 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel, ta, tb, tsa, tsb, td, p));
+    if (out_f32)
+      Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<true>, ta, tb, tsa, tsb, td, p));
+    else
+      Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<false>, ta, tb, tsa, tsb, td, p));
     return Q2B_OK;
   }
 #endif
@@ -777,7 +785,10 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 256)) return r;
     const int64_t tiles = (M / 128) * (N / 256);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    q2b::gemm_nvfp4_kernel<256><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
+    if (out_f32)
+      q2b::gemm_nvfp4_kernel<256, true><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
+    else
+      q2b::gemm_nvfp4_kernel<256, false><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
   } else {
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
     int64_t units = sp.tiles;
@@ -788,7 +799,10 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
       units = sp.tiles * sp.splits;
     }
     const int grid = static_cast<int>(units < sms ? units : sms);
-    q2b::gemm_nvfp4_kernel<128><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
+    if (out_f32)
+      q2b::gemm_nvfp4_kernel<128, true><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
+    else
+      q2b::gemm_nvfp4_kernel<128, false><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
   }
   Q2B_CUDA(cudaGetLastError());
   return Q2B_OK;
@@ -817,6 +831,14 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
   if (M > 0 && M % 128 != 0) return fail(Q2B_ERR_INVALID, "fp4_mm: M must be divisible by 128 (got %lld)", (long long)M);
   if (int r = check_gemm_args("fp4_mm", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
   return gemm_launch(D, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream);
+}
+
+int q2b_gemm_nvfp4_f32(float* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                       int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M > 0 && M % 128 != 0)
+    return fail(Q2B_ERR_INVALID, "fp4_mm_f32: M must be divisible by 128 (got %lld)", (long long)M);
+  if (int r = check_gemm_args("fp4_mm_f32", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  return gemm_launch(D, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream, true);
 }
 
 int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {

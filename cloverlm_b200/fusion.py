@@ -49,6 +49,7 @@ class _SharedInputQuartet(torch.autograd.Function):
             saved += [wq.fp4, wq.micro_scales, wq.tensor_scale]
         ctx.save_for_backward(*saved)
         ctx.hads, ctx.scratches, ctx.n, ctx.x_shape = hads, scratches, n, x.shape
+        ctx.w_f32 = [w.dtype == torch.float32 for w in weights]
         return tuple(outs)
 
     @staticmethod
@@ -64,7 +65,7 @@ class _SharedInputQuartet(torch.autograd.Function):
             if torch.is_autocast_enabled("cuda"):
                 g = g.to(torch.bfloat16)
             gi, gw = quartet_backward(g.reshape(-1, g.shape[-1]).contiguous(), xfp4, xs, xm, wfp4, ws, wm,
-                                      ctx.hads[i], ctx.scratches[i])
+                                      ctx.hads[i], ctx.scratches[i], wgrad_f32=ctx.w_f32[i])
             dx = gi if dx is None else dx + gi
             dws.append(gw)
         dx = None if dx is None else dx.reshape(ctx.x_shape)

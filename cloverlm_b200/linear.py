@@ -65,6 +65,27 @@ def _fp4_mm_fake(x_fp4, w_fp4, x_mx, w_mx, alpha):
     return torch.empty((x_fp4.shape[0], w_fp4.shape[0]), device=x_fp4.device, dtype=torch.bfloat16)
 
 
+@torch.library.custom_op("quartet2::fp4_mm_f32", mutates_args=())
+def _fp4_mm_f32(x_fp4: torch.Tensor, w_fp4: torch.Tensor, x_mx: torch.Tensor, w_mx: torch.Tensor,
+                alpha: torch.Tensor) -> torch.Tensor:
+    """_fp4_mm with an fp32 output (the accumulator times alpha, unrounded): the weight
+    gradient of an fp32 master weight, produced in the parameter's dtype (q2b_gemm_nvfp4_f32)."""
+    m, packed_k = x_fp4.shape
+    n = w_fp4.shape[0]
+    out = torch.empty([m, n], device=x_fp4.device, dtype=torch.float32)
+    if alpha.dtype != torch.float32:
+        alpha = alpha.float()
+    with torch.cuda.device(x_fp4.device):
+        _lib.call("q2b_gemm_nvfp4_f32", _lib.ptr(out), _lib.ptr(x_fp4), _lib.ptr(w_fp4), _lib.ptr(x_mx),
+                  _lib.ptr(w_mx), _lib.ptr(alpha), m, n, packed_k * 2, _lib.stream_of(x_fp4))
+    return out
+
+
+@_fp4_mm_f32.register_fake
+def _fp4_mm_f32_fake(x_fp4, w_fp4, x_mx, w_mx, alpha):
+    return torch.empty((x_fp4.shape[0], w_fp4.shape[0]), device=x_fp4.device, dtype=torch.float32)
+
+
 def to_blocked(input_matrix) -> torch.Tensor:
     """[H, W] scale matrix -> flat blocked 128x4 layout (linear.py:64-94)."""
     rows, cols = input_matrix.shape
@@ -113,6 +134,7 @@ class Quartet_II_fn(torch.autograd.Function):
         ctx.disable_backward_quant = disable_backward_quant
         ctx.scratch_amax = scratch_amax
         ctx.had = had
+        ctx.w_dtype = weight.dtype
 
         if torch.is_autocast_enabled("cuda"):
             input = input.to(torch.bfloat16)
@@ -144,13 +166,17 @@ class Quartet_II_fn(torch.autograd.Function):
             grad_output = grad_output.to(torch.bfloat16)
         flat_grad_output = grad_output.reshape(-1, grad_output.shape[-1]).contiguous()
         grad_input, grad_weight = quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, ctx.had,
-                                                   ctx.scratch_amax, ctx.disable_backward_quant)
+                                                   ctx.scratch_amax, ctx.disable_backward_quant,
+                                                   wgrad_f32=ctx.w_dtype == torch.float32)
         return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
 
 
-def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_amax, disable_backward_quant=False):
+def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_amax, disable_backward_quant=False,
+                     wgrad_f32=False):
     """dX and dW of one Quartet-II linear from the saved NVFP4 operands (linear.py:200-233):
-    rerotate H, EDEN of E and E^T (one pass), requantize W^T and X^T, two NVFP4 GEMMs."""
+    rerotate H, EDEN of E and E^T (one pass), requantize W^T and X^T, two NVFP4 GEMMs.
+    With wgrad_f32 (an fp32 master weight under autocast) dW is written in fp32 by the
+    GEMM, where the reference's bf16 dW is cast to the parameter's dtype afterwards."""
     backward_scale_override = (17 / 16) * 0.93
     had = rerotate_hadamard(had)
     if disable_backward_quant:
@@ -167,8 +193,9 @@ def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_
                          alpha=e_q.tensor_scale * wt_q.tensor_scale)
     xt_q = rht128_requant(x=xfp4, x_group_scales=xs, x_tensor_scale=xm, h=h16,
                           scale_override=backward_scale_override, scratch_amax=scratch_amax)
-    grad_weight = _fp4_mm(et_q.fp4, xt_q.fp4, et_q.micro_scales, xt_q.micro_scales,
-                          alpha=et_q.tensor_scale * xt_q.tensor_scale)
+    mm = _fp4_mm_f32 if wgrad_f32 else _fp4_mm
+    grad_weight = mm(et_q.fp4, xt_q.fp4, et_q.micro_scales, xt_q.micro_scales,
+                     alpha=et_q.tensor_scale * xt_q.tensor_scale)
     return grad_input, grad_weight
 
 

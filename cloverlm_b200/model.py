@@ -208,7 +208,8 @@ class _TiedHeadCrossEntropy(torch.autograd.Function):
             p[torch.arange(e - s, device=p.device), t] -= 1.0
             g = p.mul_(inv_n).to(torch.bfloat16)
             dh[s:e] = g @ wb
-            dw += (g.T @ hb[s:e]).float()
+            # bf16 operands, fp32 accumulation into dw in the GEMM itself
+            dw = torch.addmm(dw, g.T, hb[s:e], out_dtype=torch.float32)
         ctx.save_for_backward(dh, dw)
         ctx.h_dtype = h.dtype
         return total * inv_n

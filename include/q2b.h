@@ -171,6 +171,14 @@ int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* s
 int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                    int64_t M, int64_t N, int64_t K, void* stream);
 
+/* q2b_gemm_nvfp4 with an fp32 D[M, N] (*alpha * the fp32 accumulator, not
+ * rounded to bf16): the weight gradient of a layer whose master weight is fp32
+ * comes out in the parameter's dtype, with no separate bf16 -> fp32 pass.
+ * No counterpart in the reference (its wgrad GEMM writes bf16, which autograd
+ * then casts to the fp32 parameter's dtype). */
+int q2b_gemm_nvfp4_f32(float* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                       int64_t M, int64_t N, int64_t K, void* stream);
+
 /* q2b_gemm_nvfp4 for any M >= 1 (N a multiple of 128, K of 64), scaled by
  * *alpha times *alpha_b when alpha_b is not null (the two tensor scales,
  * so no separate product kernel runs).  A is

@@ -121,3 +121,24 @@ def test_fp4_mma_peak_probe_runs_in_range():
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     tflops = (sms // 2) * 1024 * 2.0 * 256 * 256 * 64 / (e0.elapsed_time(e1) / 1e3) / 1e12
     assert 2000 < tflops < 18000, tflops
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 1408), (4096, 3584, 2048), (896, 3584, 4096), (384, 256, 640),
+                                   (128, 896, 512)])
+def test_gemm_fp32_output_is_the_unrounded_bf16_result(M, N, K):
+    """q2b_gemm_nvfp4_f32 (fp32 D, for fp32 weight gradients) holds alpha * the fp32
+    accumulator: rounded to bf16 it equals the bf16 GEMM bit for bit, and it is within
+    the GEMM tolerance of the fp32 product of the dequantized operands."""
+    from cloverlm_b200.linear import _fp4_mm_f32
+    g = torch.Generator().manual_seed(M + N)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    b = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+    qa = quant_fp4(a, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    qb = quant_fp4(b, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    alpha = qa.tensor_scale * qb.tensor_scale
+    f32 = _fp4_mm_f32(qa.fp4, qb.fp4, qa.micro_scales, qb.micro_scales, alpha)
+    bf = _fp4_mm(qa.fp4, qb.fp4, qa.micro_scales, qb.micro_scales, alpha)
+    assert f32.dtype == torch.float32 and f32.shape == (M, N)
+    assert torch.equal(f32.to(torch.bfloat16), bf)
+    ref = _dq_exact(qa) @ _dq_exact(qb).T
+    assert ((f32 - ref).norm() / ref.norm()).item() < 1e-4  # fp32 accumulation only
