@@ -58,6 +58,7 @@ struct RhtParams {
   float inv_fp4_max;
 };
 
+
 constexpr int kRhtStages = 4;
 constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one bf16 tile
 constexpr uint32_t kHalfBytes = 128 * 128;      // one 64-column half of a tile
@@ -493,29 +494,43 @@ __device__ __forceinline__ uint32_t sr_e4m3(float in, uint32_t noise16) {
   return cvt_e4m3(__uint_as_float(bits));
 }
 
+// Eight consecutive blocked scales: scratch group i -> sf group i.
+__device__ __forceinline__ void sr8(uint2* __restrict__ sf, const uint4* __restrict__ scratch, float f, uint64_t seed,
+                                    int64_t i) {
+  const uint4 s = __ldcg(scratch + i);
+  const uint4 rnd = philox4x32_10(seed, static_cast<uint32_t>(i));
+  const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+  const uint32_t nz[4] = {rnd.x, rnd.y, rnd.z, rnd.w};
+  uint32_t o[2] = {0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float v = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16)) * f;
+    const uint32_t noise = (j & 1) ? (nz[j >> 1] >> 16) : (nz[j >> 1] & 0xFFFFu);
+    o[j >> 2] |= sr_e4m3(v, noise) << (8 * (j & 3));
+  }
+  __stcs(sf + i, make_uint2(o[0], o[1]));
+}
+
+// Tensor scale from the global max and the reciprocal the SR pass multiplies by.
+__device__ __forceinline__ float sr_factor(float max_scale, float inv_fp8_max, float* gs_out) {
+  float gs = max_scale * inv_fp8_max;
+  float f;
+  if (fabsf(gs) < FLT_MIN) { gs = 0.f; f = 0.f; } else { f = rcp_approx_ftz(gs); }
+  *gs_out = gs;
+  return f;
+}
+
 __global__ void __launch_bounds__(256) sr_scales_kernel(uint2* __restrict__ sf, float* __restrict__ ts_out,
                                                         const uint4* __restrict__ scratch,
                                                         const unsigned* __restrict__ max_bits, float inv_fp8_max,
                                                         uint64_t seed, int64_t n8) {
-  float gs = __uint_as_float(*max_bits) * inv_fp8_max;
-  float f;
-  if (fabsf(gs) < FLT_MIN) { gs = 0.f; f = 0.f; } else { f = rcp_approx_ftz(gs); }
+  float gs;
+  const float f = sr_factor(__uint_as_float(*max_bits), inv_fp8_max, &gs);
   if (blockIdx.x == 0 && threadIdx.x == 0) *ts_out = gs;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
-    const uint4 s = __ldcs(scratch + i);
-    const uint4 rnd = philox4x32_10(seed, static_cast<uint32_t>(i));
-    const uint32_t w[4] = {s.x, s.y, s.z, s.w};
-    const uint32_t nz[4] = {rnd.x, rnd.y, rnd.z, rnd.w};
-    uint32_t o[2] = {0u, 0u};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float v = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16)) * f;
-      const uint32_t noise = (j & 1) ? (nz[j >> 1] >> 16) : (nz[j >> 1] & 0xFFFFu);
-      o[j >> 2] |= sr_e4m3(v, noise) << (8 * (j & 3));
-    }
-    __stcs(sf + i, make_uint2(o[0], o[1]));
-  }
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride)
+    sr8(sf, scratch, f, seed, i);
 }
+
 
 }  // namespace q2b

@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .linear import Quartet_II_linear, _fp4_mm, quartet_backward
+from .linear import Quartet_II_linear, _fp4_mm, _quantize_weight, quartet_backward
 from .quant import NVFP4QuantMode, abs_max, quant_fp4
 
 
@@ -28,6 +28,7 @@ class _SharedInputQuartet(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, mode, input_amax, n, *args):
         weights, weight_amaxes, hads, scratches = args[:n], args[n:2 * n], args[2 * n:3 * n], args[3 * n:4 * n]
+        caches = args[4 * n:5 * n]
         if torch.is_autocast_enabled("cuda"):
             x = x.to(torch.bfloat16)
         elif x.dtype != torch.bfloat16:
@@ -37,13 +38,10 @@ class _SharedInputQuartet(torch.autograd.Function):
             input_amax = abs_max(flat)
         xq = quant_fp4(flat, amax=input_amax, scale_override=1.0, mode=mode)
         outs, saved = [], [xq.fp4, xq.micro_scales, xq.tensor_scale]
-        for w, wa in zip(weights, weight_amaxes):
-            if torch.is_autocast_enabled("cuda"):
-                w = w.to(torch.bfloat16)
-            elif w.dtype != torch.bfloat16:
+        for w, wa, cache in zip(weights, weight_amaxes, caches):
+            if not torch.is_autocast_enabled("cuda") and w.dtype != torch.bfloat16:
                 raise TypeError("Weight must be bfloat16. Either set `dtype=torch.bfloat16` or enable autocast`")
-            w = w.contiguous()
-            wq = quant_fp4(w, amax=abs_max(w) if wa is None else wa, scale_override=1.0, mode=mode)
+            wq = _quantize_weight(w, wa, mode, cache)
             y = _fp4_mm(xq.fp4, wq.fp4, xq.micro_scales, wq.micro_scales, alpha=xq.tensor_scale * wq.tensor_scale)
             outs.append(y.reshape(*x.shape[:-1], w.shape[0]))
             saved += [wq.fp4, wq.micro_scales, wq.tensor_scale]
@@ -69,7 +67,7 @@ class _SharedInputQuartet(torch.autograd.Function):
             dx = gi if dx is None else dx + gi
             dws.append(gw)
         dx = None if dx is None else dx.reshape(ctx.x_shape)
-        return (dx, None, None, None, *dws, *([None] * (3 * ctx.n)))
+        return (dx, None, None, None, *dws, *([None] * (4 * ctx.n)))
 
 
 def shared_input_forward(x: torch.Tensor, layers, input_abs_max: torch.Tensor | None = None):
@@ -82,7 +80,7 @@ def shared_input_forward(x: torch.Tensor, layers, input_abs_max: torch.Tensor | 
         raise ValueError("layers must share in_features and mode")
     n = len(layers)
     args = ([m.weight[...] for m in layers] + [m.weight_abs_max for m in layers] + [m.had for m in layers]
-            + [m.scratch_amax for m in layers])
+            + [m.scratch_amax for m in layers] + [m._weight_cache for m in layers])
     return _SharedInputQuartet.apply(x, layers[0].mode, input_abs_max, n, *args)
 
 

@@ -120,13 +120,40 @@ def _dq_fp4(x_e2m1: torch.Tensor, x_e4m3: torch.Tensor, alpha):
     return out.to(torch.bfloat16)
 
 
+def _quantize_weight(weight, weight_amax, mode, cache):
+    """bf16 (under autocast), abs-max and NVFP4 quantization of a layer weight.
+
+    `cache` (a dict owned by the layer, or None) keeps the result while the weight is
+    unchanged: it is keyed by the weight's storage pointer, its autograd version counter
+    (bumped by every in-place update, including QuartetAdamW's) and the identity of the
+    abs-max tensor the optimizer hands over each step.  The reference quantizes the weight
+    in every forward; the result is identical, so a step with several micro-batches
+    quantizes each weight once."""
+    key = None
+    if cache is not None and not torch.compiler.is_compiling():
+        key = (weight.data_ptr(), weight._version, id(weight_amax) if weight_amax is not None else None)
+        hit = cache.get("q")
+        if hit is not None and cache.get("key") == key:
+            return hit
+    w = weight
+    if torch.is_autocast_enabled("cuda"):
+        w = w.to(torch.bfloat16)
+    w = w.contiguous()
+    if weight_amax is None:
+        weight_amax = abs_max(w)
+    q = quant_fp4(w, amax=weight_amax, scale_override=1.0, mode=mode)
+    if key is not None:
+        cache["q"], cache["key"] = q, key
+    return q
+
+
 class Quartet_II_fn(torch.autograd.Function):
     group_size = 16
 
     @staticmethod
     def forward(ctx, input, weight, had, mode: NVFP4QuantMode, disable_backward_quant: bool = False,
                 weight_amax: torch.Tensor = None, input_amax: torch.Tensor = None,
-                scratch_amax: torch.Tensor = None):
+                scratch_amax: torch.Tensor = None, weight_cache: dict = None):
         ctx.batch = input.shape[0]
         ctx.seq = input.shape[1]
         ctx.in_dim = weight.shape[1]
@@ -136,9 +163,9 @@ class Quartet_II_fn(torch.autograd.Function):
         ctx.had = had
         ctx.w_dtype = weight.dtype
 
+        weight_in = weight
         if torch.is_autocast_enabled("cuda"):
             input = input.to(torch.bfloat16)
-            weight = weight.to(torch.bfloat16)
         elif weight.dtype != torch.bfloat16:
             raise TypeError("Weight must be bfloat16. Either set `dtype=torch.bfloat16` or enable autocast`")
         elif input.dtype != torch.bfloat16:
@@ -146,13 +173,10 @@ class Quartet_II_fn(torch.autograd.Function):
 
         forward_scale_override = 1.0
         flat_input = input.reshape(-1, input.shape[-1]).contiguous()
-        weight = weight.contiguous()
         if input_amax is None:
             input_amax = abs_max(flat_input)
-        if weight_amax is None:
-            weight_amax = abs_max(weight)
         input_fp4 = quant_fp4(flat_input, amax=input_amax, scale_override=forward_scale_override, mode=mode)
-        weight_fp4 = quant_fp4(weight, amax=weight_amax, scale_override=forward_scale_override, mode=mode)
+        weight_fp4 = _quantize_weight(weight_in, weight_amax, mode, weight_cache)
         ctx.save_for_backward(input_fp4.fp4, input_fp4.micro_scales, input_fp4.tensor_scale,
                               weight_fp4.fp4, weight_fp4.micro_scales, weight_fp4.tensor_scale)
         res = _fp4_mm(input_fp4.fp4, weight_fp4.fp4, input_fp4.micro_scales, weight_fp4.micro_scales,
@@ -168,7 +192,7 @@ class Quartet_II_fn(torch.autograd.Function):
         grad_input, grad_weight = quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, ctx.had,
                                                    ctx.scratch_amax, ctx.disable_backward_quant,
                                                    wgrad_f32=ctx.w_dtype == torch.float32)
-        return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None
+        return grad_input.reshape(ctx.batch, ctx.seq, ctx.in_dim), grad_weight, None, None, None, None, None, None, None
 
 
 def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_amax, disable_backward_quant=False,
@@ -213,6 +237,7 @@ class Quartet_II_linear(torch.nn.Linear):
         self.register_buffer("had", had, persistent=False)
         self.register_buffer("scratch_amax", torch.empty((), dtype=torch.uint32, device=self.weight.device),
                              persistent=False)
+        self._weight_cache = {}  # the weight's NVFP4 quantization while it is unchanged (_quantize_weight)
 
     def _apply(self, fn):
         old_device = self.weight.device
@@ -223,7 +248,7 @@ class Quartet_II_linear(torch.nn.Linear):
 
     def forward(self, x, disable_backward_quant=False, input_abs_max=None):
         return Quartet_II_fn.apply(x, self.weight[...], self.had, self.mode, disable_backward_quant,
-                                   self.weight_abs_max, input_abs_max, self.scratch_amax)
+                                   self.weight_abs_max, input_abs_max, self.scratch_amax, self._weight_cache)
 
 
 def register_optimizer_hook(model: torch.nn.Module, optimizer: torch.optim.Optimizer):

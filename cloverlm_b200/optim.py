@@ -74,6 +74,8 @@ class QuartetAdamW(torch.optim.Optimizer):
                               _lib.ptr(g), int(g.dtype == torch.bfloat16), p.numel(), float(group["lr"]),
                               float(beta1), float(beta2), float(group["eps"]), float(group["weight_decay"]),
                               int(state["step"]), None, _lib.ptr(amax), _lib.stream_of(p))
+                # the update is not a torch op: record it, so caches keyed by the version see it
+                torch.autograd.graph.increment_version(p)
                 if mod is not None:
                     mod.weight_abs_max = amax
                 device = p.device

@@ -185,3 +185,39 @@ def test_training_step_captures_in_a_cuda_graph():
         for got, ref in ((gx, exact[0]), (gw, exact[1])):
             _, bits, cos = _quality(got, ref)
             assert bits > 1.7 and abs(cos - 1.0) < 0.1, (bits, cos)
+
+
+def test_weight_quantization_is_reused_only_while_the_weight_is_unchanged():
+    """Quartet_II_linear keeps its weight's NVFP4 quantization between forwards (a step's
+    micro-batches quantize each weight once); any update -- an in-place torch op, a
+    QuartetAdamW step, a new abs-max from the optimizer -- makes the next forward
+    quantize again, so outputs always equal a fresh quantization."""
+    from cloverlm_b200.optim import QuartetAdamW
+    torch.manual_seed(5)
+    lin = Quartet_II_linear(256, 384, bias=False, device="cuda")
+    x = torch.randn(1, 128, 256, device="cuda")
+
+    def fresh():
+        lin._weight_cache.clear()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            return lin(x)
+
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y0 = lin(x)
+        q0 = lin._weight_cache["q"]
+        y1 = lin(x)
+    assert lin._weight_cache["q"] is q0 and torch.equal(y0, y1)
+    with torch.no_grad():
+        lin.weight.mul_(1.5)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y2 = lin(x)
+    assert lin._weight_cache["q"] is not q0 and torch.equal(y2, fresh())
+    opt = QuartetAdamW(lin.parameters(), lr=1e-2)
+    opt.attach(lin)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        lin(x).float().pow(2).mean().backward()
+    q1 = lin._weight_cache["q"]
+    opt.step()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y3 = lin(x)
+    assert lin._weight_cache["q"] is not q1 and torch.equal(y3, fresh())
