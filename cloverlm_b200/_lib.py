@@ -41,6 +41,9 @@ SIGNATURES = {
     "q2b_rht_requant": [_P, _P, _P, _P, _P, _P, _INT, _P, _P, _P, _U64, _F, _F, _I64, _I64, _P],
     "q2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "q2b_gemm_nvfp4_f32": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "q2b_gemm_nvfp4_add": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "q2b_gemm_nvfp4_relu2": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "q2b_gemm_nvfp4_relu2_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "q2b_quant_fwd_ragged": [_P, _P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_gemm_nvfp4_ex": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P],
     "q2b_quant_rows_fused": [_P, _P, _P, _P, _F, _I64, _I64, _INT, _P],

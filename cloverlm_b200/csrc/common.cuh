@@ -524,6 +524,14 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
                : "memory");
 }
+// TMA tensor reduction shared -> global: the box is added element-wise into global memory
+// (the tensor map's element type; local memory only), tracked as a bulk group.
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   tmap),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the thread's bulk stores have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {

@@ -32,6 +32,8 @@ struct GemmParams {
   const float* alpha;
   const float* alpha_b; // optional second factor of alpha (nullptr = 1)
   void* D;              // [m_valid, N] row-major, bf16 (or fp32 for the kOutF32 kernels)
+  const uint16_t* aux;  // kEpiRelu2Bwd: the MLP pre-activation a, bf16 [M, N] row-major
+  unsigned* amax;       // kEpiRelu2: max |relu(D)^2| (fp32 bits, atomicMax; zeroed by the launcher)
   int64_t m_valid;      // rows of A and D that exist (A rows past it read as zero through TMA)
   int splits;           // K split into this many ranges per output tile (1 = none)
   float* ws;            // splits > 1: fp32 partial tiles [tiles][128][BN], zero between calls
@@ -78,7 +80,7 @@ struct GemmCfg {
 // copies issued by a second warp overlap the MMAs of earlier stages.  Column
 // set s is free again when full[s] fires, because the producer reloads stage
 // s only after the MMAs that read set s have completed (empty[s]).
-template <int BN, bool kOutF32 = false>
+template <int BN, bool kOutF32 = false, bool kAccum = false>
 __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const GemmParams p) {
@@ -369,8 +371,26 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < kChunks; ++ch) {
           uint4* dst = reinterpret_cast<uint4*>(drow + ch * 32);
+          if constexpr (kAccum) {
+            // D += bf16(alpha * acc): bf16 adds of the existing output (the row is this lane's)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
+            for (int k = 0; k < 4; ++k) {
+              const uint4 d = dst[k];
+              const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
+              uint32_t sum[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t v = o[ch][4 * k + j];
+                sum[j] = pack_bf16x2(__uint_as_float(dw[j] << 16) + __uint_as_float(v << 16),
+                                     __uint_as_float(dw[j] & 0xFFFF0000u) + __uint_as_float(v & 0xFFFF0000u));
+              }
+              dst[k] = make_uint4(sum[0], sum[1], sum[2], sum[3]);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              dst[k] = make_uint4(o[ch][4 * k], o[ch][4 * k + 1], o[ch][4 * k + 2], o[ch][4 * k + 3]);
+          }
         }
       }
     }
@@ -473,12 +493,27 @@ __device__ __forceinline__ void tc_commit_pair_leader(uint64_t* bar) {
 //      order; on its group's K blocks it issues its third of the stage's cta_group::2
 //      tcgen05.cp into TMEM set s and commits sfready[s] (three arrivals complete it)
 //   kEpiWarp0+  epilogue: drains its own TMEM rows, arrives on the leader's tempty
-template <bool kOutF32 = false>
+// Epilogues of the pair kernel (D = alpha * A B^T is formed in fp32 first):
+//   kEpiBf16      D bf16
+//   kEpiF32       D fp32 (weight gradients of fp32 master weights)
+//   kEpiRelu2     D = bf16(alpha*acc), the MLP pre-activation a, and D2 = bf16(relu(a)^2), the
+//                 activation the next Quartet layer quantizes, plus *amax = max D2: the MLP's
+//                 first linear, its ReLU^2 and the second linear's input abs-max in one pass
+//                 (src/models/mlp.py:34-38,113-118)
+//   kEpiRelu2Bwd  D = bf16(2 * relu(a) * bf16(alpha*acc)) with a = aux: the second linear's
+//                 dgrad followed by the ReLU^2 backward, without writing and re-reading dH
+//   kEpiBf16Add   D += bf16(alpha*acc), added in place by TMA reductions: the input gradient of
+//                 several layers that read one activation (Q, K and V) summed in the dgrad GEMMs
+enum GemmEpi : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiRelu2 = 2, kEpiRelu2Bwd = 3, kEpiBf16Add = 4 };
+
+template <int kEpi = kEpiBf16>
 __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     gemm_nvfp4_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ CUtensorMap tmap_d, const GemmParams p) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_d2,
+                          const GemmParams p) {
   using Cfg = Gemm2Cfg;
+  constexpr bool kOutF32 = kEpi == kEpiF32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
@@ -667,6 +702,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     const float alpha = *p.alpha * (p.alpha_b != nullptr ? *p.alpha_b : 1.f);
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
     uint8_t* stage = smem + Cfg::kStagingOff + e * Cfg::kStagingPerWarp;
+    float relu2_max = 0.f;
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
       // tile coordinates before the wait: the drain is on the MMA's critical path
@@ -693,18 +729,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
       if (e == 0) { Q2B_S_ADD(8, _e2 - _e1) Q2B_S_ADD(9, _e3 - _e2) Q2B_S_ADD(10, _e4 - _e3) Q2B_S_ADD(11, _e5 - _e4) }
       // one box = 32 rows x 64 bytes: 32 bf16 columns, or 16 fp32 columns
       constexpr int kBoxCols = kOutF32 ? 16 : 32;
-#pragma unroll
-      for (int bx = 0; bx < kCols / kBoxCols; ++bx) {
-        uint32_t o[16];
-        if constexpr (kOutF32) {
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            o[k] = __float_as_uint(__uint_as_float(r[bx >> 1][16 * (bx & 1) + k]) * alpha);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            o[k] = pack_bf16x2(__uint_as_float(r[bx][2 * k]) * alpha, __uint_as_float(r[bx][2 * k + 1]) * alpha);
-        }
+      // write one box of this warp's rows through the staging buffer with a TMA store
+      auto store_box = [&](const uint32_t (&o)[16], const CUtensorMap* map, int col) {
         // the previous box's store must have read the staging buffer
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
@@ -715,13 +741,64 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmap_d, stage, static_cast<int>(tn * 256 + c0 + bx * kBoxCols), row0);
+          if constexpr (kEpi == kEpiBf16Add)
+            tma_reduce_add_2d(map, stage, col, row0);
+          else
+            tma_store_2d(map, stage, col, row0);
           bulk_commit_group();
+        }
+      };
+#pragma unroll
+      for (int bx = 0; bx < kCols / kBoxCols; ++bx) {
+        const int col = static_cast<int>(tn * 256 + c0 + bx * kBoxCols);
+        uint32_t o[16];
+        if constexpr (kOutF32) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o[k] = __float_as_uint(__uint_as_float(r[bx >> 1][16 * (bx & 1) + k]) * alpha);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o[k] = pack_bf16x2(__uint_as_float(r[bx][2 * k]) * alpha, __uint_as_float(r[bx][2 * k + 1]) * alpha);
+        }
+        if constexpr (kEpi == kEpiRelu2Bwd) {
+          // da = 2 * relu(a) * g, g the bf16 dgrad value, a this lane's row of the pre-activation
+          const uint4* ap = reinterpret_cast<const uint4*>(p.aux + static_cast<int64_t>(row0 + lane) * p.N + col);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 av = __ldg(ap + k);
+            const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t g = o[4 * k + j];
+              const float a0 = fmaxf(__uint_as_float(aw[j] << 16), 0.f);
+              const float a1 = fmaxf(__uint_as_float(aw[j] & 0xFFFF0000u), 0.f);
+              o[4 * k + j] = pack_bf16x2(2.f * a0 * __uint_as_float(g << 16),
+                                         2.f * a1 * __uint_as_float(g & 0xFFFF0000u));
+            }
+          }
+        }
+        store_box(o, &tmap_d, col);
+        if constexpr (kEpi == kEpiRelu2) {
+          // h = relu(a)^2 from the bf16 pre-activation just stored
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float a0 = fmaxf(__uint_as_float(o[k] << 16), 0.f);
+            const float a1 = fmaxf(__uint_as_float(o[k] & 0xFFFF0000u), 0.f);
+            o[k] = pack_bf16x2(a0 * a0, a1 * a1);
+            relu2_max = fmaxf(relu2_max, fmaxf(__uint_as_float(o[k] << 16), __uint_as_float(o[k] & 0xFFFF0000u)));
+          }
+          store_box(o, &tmap_d2, col);
         }
       }
     }
     if (lane == 0) bulk_wait_group0();
     __syncwarp();
+    if constexpr (kEpi == kEpiRelu2) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) relu2_max = fmaxf(relu2_max, __shfl_xor_sync(0xffffffffu, relu2_max, o));
+      if (lane == 0) atomicMax(p.amax, __float_as_uint(relu2_max));
+    }
   }
 
 #ifdef Q2B_GEMM2_STATS

@@ -312,9 +312,9 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
 }
 
 // ---------------------------------------------------------------- ReLU^2 grad
-// da = bf16(2 * relu(a) * g) for n bf16 values (n a multiple of 8).
-__global__ void __launch_bounds__(256) relu2_bwd_kernel(uint4* __restrict__ da, const uint4* __restrict__ a,
-                                                        const uint4* __restrict__ g, int64_t nvec) {
+// da = bf16(2 * relu(a) * g) for n bf16 values (n a multiple of 8); da may be g.
+__global__ void __launch_bounds__(256) relu2_bwd_kernel(uint4* da, const uint4* __restrict__ a, const uint4* g,
+                                                        int64_t nvec) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += stride) {
     const uint4 av = __ldcs(a + i), gv = __ldcs(g + i);

@@ -104,8 +104,13 @@ int device_setup(int* dev_out, int* sms_out) {
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128, false>, GemmCfg<128>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256, true>, GemmCfg<256>::kSmemBytes));
     Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128, true>, GemmCfg<128>::kSmemBytes));
-    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<false>, Gemm2Cfg::kSmemBytes));
-    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<true>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<kEpiBf16>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<kEpiF32>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<kEpiRelu2>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<kEpiRelu2Bwd>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_2sm_kernel<kEpiBf16Add>, Gemm2Cfg::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<256, false, true>, GemmCfg<256>::kSmemBytes));
+    Q2B_CUDA(set_smem(gemm_nvfp4_kernel<128, false, true>, GemmCfg<128>::kSmemBytes));
     Q2B_CUDA(set_smem(fp4_mma_peak_kernel, PeakCfg::kSmemBytes));
     d.ready = true;
   }
@@ -731,26 +736,42 @@ int64_t split_ws_bytes(const SplitPlan& sp) {
   return sp.tiles * 128 * 128 * 4 + sp.tiles * q2b::GemmCfg<128>::kEpiWarps * 4;
 }
 
+// Whether the 2-SM pair kernel takes this problem (256-aligned, enough tiles to fill the pairs).
+bool takes_pair_kernel(int64_t m_valid, int64_t N, int sms, const void* D) {
+  const int64_t M = (m_valid + 127) / 128 * 128;
+  return m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms &&
+         (reinterpret_cast<uintptr_t>(D) & 15u) == 0;
+}
+
 int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                 const float* alpha_b, int64_t m_valid, int64_t N, int64_t K, void* ws, int64_t ws_bytes,
-                void* stream, bool out_f32 = false) {
+                void* stream, bool out_f32 = false, int epi = q2b::kEpiBf16, void* D2 = nullptr,
+                const void* aux = nullptr, float* amax = nullptr) {
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t M = (m_valid + 127) / 128 * 128;
   CUtensorMap ta, tb;
   q2b::GemmParams p{M, N, K, static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb), alpha, alpha_b,
-                    D, m_valid, 1, nullptr, nullptr};
+                    D, static_cast<const uint16_t*>(aux), reinterpret_cast<unsigned*>(amax), m_valid, 1, nullptr,
+                    nullptr};
+  if (out_f32) epi = q2b::kEpiF32;
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
-  if (m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms &&
-      (reinterpret_cast<uintptr_t>(D) & 15u) == 0) {
+  if (takes_pair_kernel(m_valid, N, sms, D)) {
     // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair; D written by TMA stores
     CUtensorMap tsa, tsb, td;
     // store boxes of 32 rows x 64 bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle
+    CUtensorMap td2;
     if (int r = out_f32 ? make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                         : make_tmap(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return r;
+    if (epi == q2b::kEpiRelu2) {
+      if (int r = make_tmap(&td2, D2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return r;
+    } else {
+      td2 = td;
+    }
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 128)) return r;
     if (int r = make_tmap(&tsa, sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, M * K / 16 / 256, 256, 8,
                           CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -772,21 +793,36 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (out_f32)
-      Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<true>, ta, tb, tsa, tsb, td, p));
-    else
-      Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<false>, ta, tb, tsa, tsb, td, p));
+    switch (epi) {
+      case q2b::kEpiF32:
+        Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<q2b::kEpiF32>, ta, tb, tsa, tsb, td, td2, p));
+        break;
+      case q2b::kEpiRelu2:
+        Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<q2b::kEpiRelu2>, ta, tb, tsa, tsb, td, td2, p));
+        break;
+      case q2b::kEpiRelu2Bwd:
+        Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<q2b::kEpiRelu2Bwd>, ta, tb, tsa, tsb, td, td2, p));
+        break;
+      case q2b::kEpiBf16Add:
+        Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<q2b::kEpiBf16Add>, ta, tb, tsa, tsb, td, td2, p));
+        break;
+      default:
+        Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::gemm_nvfp4_2sm_kernel<q2b::kEpiBf16>, ta, tb, tsa, tsb, td, td2, p));
+    }
     return Q2B_OK;
   }
 #endif
+  const bool accum = epi == q2b::kEpiBf16Add;
   const SplitPlan sp = plan_split(m_valid, N, K, sms);
-  const bool split = sp.splits > 1 && ws != nullptr && ws_bytes >= split_ws_bytes(sp);
+  const bool split = !accum && sp.splits > 1 && ws != nullptr && ws_bytes >= split_ws_bytes(sp);
   if (N % 256 == 0 && !split && (M / 128) * (N / 256) * 2 >= sms) {
     if (int r = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, 128, 256)) return r;
     const int64_t tiles = (M / 128) * (N / 256);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
     if (out_f32)
       q2b::gemm_nvfp4_kernel<256, true><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
+    else if (accum)
+      q2b::gemm_nvfp4_kernel<256, false, true><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
     else
       q2b::gemm_nvfp4_kernel<256, false><<<grid, q2b::GemmCfg<256>::kThreads, q2b::GemmCfg<256>::kSmemBytes, st>>>(ta, tb, p);
   } else {
@@ -801,6 +837,8 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     const int grid = static_cast<int>(units < sms ? units : sms);
     if (out_f32)
       q2b::gemm_nvfp4_kernel<128, true><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
+    else if (accum)
+      q2b::gemm_nvfp4_kernel<128, false, true><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
     else
       q2b::gemm_nvfp4_kernel<128, false><<<grid, q2b::GemmCfg<128>::kThreads, q2b::GemmCfg<128>::kSmemBytes, st>>>(ta, tb, p);
   }
@@ -839,6 +877,49 @@ int q2b_gemm_nvfp4_f32(float* D, const void* A, const void* B, const void* sfa, 
     return fail(Q2B_ERR_INVALID, "fp4_mm_f32: M must be divisible by 128 (got %lld)", (long long)M);
   if (int r = check_gemm_args("fp4_mm_f32", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
   return gemm_launch(D, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream, true);
+}
+
+int q2b_gemm_nvfp4_add(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                       int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M > 0 && M % 128 != 0)
+    return fail(Q2B_ERR_INVALID, "fp4_mm_add: M must be divisible by 128 (got %lld)", (long long)M);
+  if (int r = check_gemm_args("fp4_mm_add", D, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  return gemm_launch(D, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream, false, q2b::kEpiBf16Add);
+}
+
+int q2b_gemm_nvfp4_relu2(void* A_out, void* H_out, float* amax, const void* A, const void* B, const void* sfa,
+                         const void* sfb, const float* alpha, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M > 0 && M % 128 != 0)
+    return fail(Q2B_ERR_INVALID, "fp4_mm_relu2: M must be divisible by 128 (got %lld)", (long long)M);
+  if (int r = check_gemm_args("fp4_mm_relu2", A_out, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  Q2B_REQUIRE_PTR(H_out);
+  Q2B_REQUIRE_NONNULL(amax);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Q2B_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
+  if (takes_pair_kernel(M, N, sms, A_out))
+    return gemm_launch(A_out, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream, false, q2b::kEpiRelu2,
+                       H_out, nullptr, amax);
+  // other shapes: the GEMM, then the one-pass ReLU^2 + abs-max kernel (same results)
+  if (int r = gemm_launch(A_out, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream)) return r;
+  return q2b_relu2_abs_max(H_out, amax, A_out, M * N, stream);
+}
+
+int q2b_gemm_nvfp4_relu2_bwd(void* dA, const void* a, const void* A, const void* B, const void* sfa, const void* sfb,
+                             const float* alpha, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M > 0 && M % 128 != 0)
+    return fail(Q2B_ERR_INVALID, "fp4_mm_relu2_bwd: M must be divisible by 128 (got %lld)", (long long)M);
+  if (int r = check_gemm_args("fp4_mm_relu2_bwd", dA, A, B, sfa, sfb, alpha, M, N, K)) return r;
+  Q2B_REQUIRE_PTR(a);
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  if (takes_pair_kernel(M, N, sms, dA))
+    return gemm_launch(dA, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream, false, q2b::kEpiRelu2Bwd,
+                       nullptr, a, nullptr);
+  // other shapes: the GEMM into dA, then the ReLU^2 backward in place
+  if (int r = gemm_launch(dA, A, B, sfa, sfb, alpha, nullptr, M, N, K, nullptr, 0, stream)) return r;
+  return q2b_relu2_bwd(dA, a, dA, M * N, stream);
 }
 
 int64_t q2b_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {

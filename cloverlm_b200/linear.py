@@ -86,6 +86,45 @@ def _fp4_mm_f32_fake(x_fp4, w_fp4, x_mx, w_mx, alpha):
     return torch.empty((x_fp4.shape[0], w_fp4.shape[0]), device=x_fp4.device, dtype=torch.float32)
 
 
+def _fp4_mm_add(out, x_fp4, w_fp4, x_mx, w_mx, alpha):
+    """out += _fp4_mm(...) in place (bf16 adds; q2b_gemm_nvfp4_add); returns out."""
+    m, packed_k = x_fp4.shape
+    n = w_fp4.shape[0]
+    assert out.dtype == torch.bfloat16 and out.is_contiguous() and out.shape == (m, n)
+    alpha = alpha.float()
+    with torch.cuda.device(x_fp4.device):
+        _lib.call("q2b_gemm_nvfp4_add", _lib.ptr(out), _lib.ptr(x_fp4), _lib.ptr(w_fp4), _lib.ptr(x_mx),
+                  _lib.ptr(w_mx), _lib.ptr(alpha), m, n, packed_k * 2, _lib.stream_of(x_fp4))
+    return out
+
+
+def _fp4_mm_relu2(x_fp4, w_fp4, x_mx, w_mx, alpha):
+    """(a, relu(a)^2, max relu(a)^2) for a = _fp4_mm(...) in one GEMM (q2b_gemm_nvfp4_relu2)."""
+    m, packed_k = x_fp4.shape
+    n = w_fp4.shape[0]
+    a = torch.empty([m, n], device=x_fp4.device, dtype=torch.bfloat16)
+    h = torch.empty_like(a)
+    amax = torch.empty((), device=x_fp4.device, dtype=torch.float32)
+    alpha = alpha.float()
+    with torch.cuda.device(x_fp4.device):
+        _lib.call("q2b_gemm_nvfp4_relu2", _lib.ptr(a), _lib.ptr(h), _lib.ptr(amax), _lib.ptr(x_fp4), _lib.ptr(w_fp4),
+                  _lib.ptr(x_mx), _lib.ptr(w_mx), _lib.ptr(alpha), m, n, packed_k * 2, _lib.stream_of(x_fp4))
+    return a, h, amax
+
+
+def _fp4_mm_relu2_bwd(x_fp4, w_fp4, x_mx, w_mx, alpha, a):
+    """2 * relu(a) * _fp4_mm(...) in one GEMM (q2b_gemm_nvfp4_relu2_bwd); a bf16 [m, n]."""
+    m, packed_k = x_fp4.shape
+    n = w_fp4.shape[0]
+    a = a.reshape(m, n).contiguous()
+    out = torch.empty([m, n], device=x_fp4.device, dtype=torch.bfloat16)
+    alpha = alpha.float()
+    with torch.cuda.device(x_fp4.device):
+        _lib.call("q2b_gemm_nvfp4_relu2_bwd", _lib.ptr(out), _lib.ptr(a), _lib.ptr(x_fp4), _lib.ptr(w_fp4),
+                  _lib.ptr(x_mx), _lib.ptr(w_mx), _lib.ptr(alpha), m, n, packed_k * 2, _lib.stream_of(x_fp4))
+    return out
+
+
 def to_blocked(input_matrix) -> torch.Tensor:
     """[H, W] scale matrix -> flat blocked 128x4 layout (linear.py:64-94)."""
     rows, cols = input_matrix.shape
@@ -196,11 +235,15 @@ class Quartet_II_fn(torch.autograd.Function):
 
 
 def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_amax, disable_backward_quant=False,
-                     wgrad_f32=False):
+                     wgrad_f32=False, relu2_input=None, grad_input_acc=None):
     """dX and dW of one Quartet-II linear from the saved NVFP4 operands (linear.py:200-233):
     rerotate H, EDEN of E and E^T (one pass), requantize W^T and X^T, two NVFP4 GEMMs.
     With wgrad_f32 (an fp32 master weight under autocast) dW is written in fp32 by the
-    GEMM, where the reference's bf16 dW is cast to the parameter's dtype afterwards."""
+    GEMM, where the reference's bf16 dW is cast to the parameter's dtype afterwards.
+    With relu2_input (the pre-activation a of an input x = relu(a)^2) the dgrad GEMM's
+    epilogue applies the ReLU^2 backward and the result is dL/da instead of dL/dx.  With
+    grad_input_acc (a bf16 [M, K] tensor) dX is added into it by the dgrad GEMM, which
+    returns it."""
     backward_scale_override = (17 / 16) * 0.93
     had = rerotate_hadamard(had)
     if disable_backward_quant:
@@ -213,8 +256,15 @@ def quartet_backward(flat_grad_output, xfp4, xs, xm, wfp4, ws, wm, had, scratch_
                                        scratch_amax=scratch_amax)
     wt_q = rht128_requant(x=wfp4, x_group_scales=ws, x_tensor_scale=wm, h=h16,
                           scale_override=backward_scale_override, scratch_amax=scratch_amax)
-    grad_input = _fp4_mm(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
-                         alpha=e_q.tensor_scale * wt_q.tensor_scale)
+    if grad_input_acc is not None:
+        grad_input = _fp4_mm_add(grad_input_acc, e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
+                                 e_q.tensor_scale * wt_q.tensor_scale)
+    elif relu2_input is None:
+        grad_input = _fp4_mm(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
+                             alpha=e_q.tensor_scale * wt_q.tensor_scale)
+    else:
+        grad_input = _fp4_mm_relu2_bwd(e_q.fp4, wt_q.fp4, e_q.micro_scales, wt_q.micro_scales,
+                                       e_q.tensor_scale * wt_q.tensor_scale, relu2_input)
     xt_q = rht128_requant(x=xfp4, x_group_scales=xs, x_tensor_scale=xm, h=h16,
                           scale_override=backward_scale_override, scratch_amax=scratch_amax)
     mm = _fp4_mm_f32 if wgrad_f32 else _fp4_mm

@@ -23,8 +23,9 @@ B200 layout of the work: the three projections of a block quantize X once
 (fusion.shared_input_forward); RoPE + sphere norm + scale is one libq2b kernel per
 direction (q2b_rope_norm_fwd / _bwd); each residual RMSNorm writes the fp32 residual,
 its bf16 copy and that copy's abs-max in one pass (q2b_add_rmsnorm_amax), so the next
-Quartet layer skips its abs-max read; ReLU^2 and its abs-max are one pass forward
-(q2b_relu2_abs_max) and one backward (q2b_relu2_bwd); attention is cuDNN's fused
+Quartet layer skips its abs-max read; the MLP's ReLU^2 and its abs-max come out of the first
+linear's GEMM epilogue and its gradient out of the second linear's dgrad epilogue
+(fusion.mlp_relu2); attention is cuDNN's fused
 kernel through torch SDPA (a library call, like the reference's FlashAttention);
 the tied head and cross-entropy run in row chunks so no full [tokens, vocab]
 logit matrix is ever stored.
@@ -39,7 +40,7 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import _lib
-from .fusion import relu2_abs_max, shared_input_forward
+from .fusion import mlp_relu2, shared_input_forward
 from .linear import Quartet_II_linear
 from .quant import abs_max
 
@@ -251,9 +252,7 @@ class Block(torch.nn.Module):
         o = o.transpose(1, 2).reshape(B, T, cfg.d)
         y = self.lo(o)
         x, xb, amax = add_rmsnorm_amax(x, y, self.att_norm, cfg.norm_eps)
-        a = self.l1(xb, input_abs_max=amax)
-        h, hamax = relu2_abs_max(a)
-        z = self.l2(h, input_abs_max=hamax)
+        z = mlp_relu2(xb, self.l1, self.l2, input_abs_max=amax)
         return add_rmsnorm_amax(x, z, self.mlp_norm, cfg.norm_eps)
 
 

@@ -179,6 +179,33 @@ int q2b_gemm_nvfp4(void* D, const void* A, const void* B, const void* sfa, const
 int q2b_gemm_nvfp4_f32(float* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
                        int64_t M, int64_t N, int64_t K, void* stream);
 
+/* D += bf16(*alpha * A B^T) for a bf16 D [M, N] that already holds a value:
+ * each element becomes the bf16 sum of the old value and the bf16-rounded
+ * product (TMA reductions on the 2-SM path).  Used to sum the input gradients
+ * of the layers that read one activation (the attention projections).
+ * Replaces: dx = dx_q + dx_k + dx_v, the autograd accumulation of the three
+ * projections' input gradients (src/models/transformer.py:341-344). */
+int q2b_gemm_nvfp4_add(void* D, const void* A, const void* B, const void* sfa, const void* sfb, const float* alpha,
+                       int64_t M, int64_t N, int64_t K, void* stream);
+
+/* The MLP's first linear with its activation in the GEMM epilogue: A_out =
+ * bf16(*alpha * A B^T) (the pre-activation a, [M, N]), H_out = bf16(relu(a)^2)
+ * and *amax = max H_out (fp32, written by the call).  Shapes as
+ * q2b_gemm_nvfp4; shapes the 2-SM kernel does not take run the GEMM and then
+ * q2b_relu2_abs_max (same results).
+ * Replaces: l1 = Quartet_II_linear -> ReLU2 -> abs_max of the l2 input,
+ * src/models/mlp.py:34-38,113-118, quartet2/python/quartet2/linear.py:179-183. */
+int q2b_gemm_nvfp4_relu2(void* A_out, void* H_out, float* amax, const void* A, const void* B, const void* sfa,
+                         const void* sfb, const float* alpha, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* The second MLP linear's dgrad with the ReLU^2 backward in the epilogue:
+ * dA = bf16(2 * relu(a) * bf16(*alpha * A B^T)), a the saved pre-activation
+ * (bf16 [M, N]).  Other shapes: the GEMM, then q2b_relu2_bwd in place.
+ * Replaces: the dX GEMM of l2's backward (linear.py:222-225) followed by the
+ * autograd backward of relu(x)**2 (src/models/mlp.py:34-38). */
+int q2b_gemm_nvfp4_relu2_bwd(void* dA, const void* a, const void* A, const void* B, const void* sfa, const void* sfb,
+                             const float* alpha, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* q2b_gemm_nvfp4 for any M >= 1 (N a multiple of 128, K of 64), scaled by
  * *alpha times *alpha_b when alpha_b is not null (the two tensor scales,
  * so no separate product kernel runs).  A is

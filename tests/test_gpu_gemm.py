@@ -142,3 +142,23 @@ def test_gemm_fp32_output_is_the_unrounded_bf16_result(M, N, K):
     assert torch.equal(f32.to(torch.bfloat16), bf)
     ref = _dq_exact(qa) @ _dq_exact(qb).T
     assert ((f32 - ref).norm() / ref.norm()).item() < 1e-4  # fp32 accumulation only
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 1408), (4096, 3584, 896), (384, 256, 640)])
+def test_gemm_add_accumulates_into_the_output(M, N, K):
+    """q2b_gemm_nvfp4_add: D += bf16(alpha * A B^T), each element the bf16 sum of the old value and
+    the bf16 GEMM result (TMA reductions on the 2-SM path, bf16 adds on the 1-SM path): equal to
+    (D + _fp4_mm(...)) in bf16 up to one rounding step in at most 1e-3 of the elements."""
+    from cloverlm_b200.linear import _fp4_mm_add
+    g = torch.Generator().manual_seed(M + K)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    b = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+    d0 = torch.randn(M, N, generator=g).to(torch.bfloat16).cuda()
+    qa = quant_fp4(a, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    qb = quant_fp4(b, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    alpha = qa.tensor_scale * qb.tensor_scale
+    got = _fp4_mm_add(d0.clone(), qa.fp4, qb.fp4, qa.micro_scales, qb.micro_scales, alpha)
+    want = (d0.float() + _fp4_mm(qa.fp4, qb.fp4, qa.micro_scales, qb.micro_scales, alpha).float()).to(torch.bfloat16)
+    diff = (got.view(torch.int16).int() - want.view(torch.int16).int()).abs()
+    assert int(diff.max()) <= 1 and (diff != 0).float().mean().item() <= 1e-3
+    assert _lib.device_status() == 0

@@ -221,3 +221,32 @@ def test_weight_quantization_is_reused_only_while_the_weight_is_unchanged():
     with torch.autocast("cuda", dtype=torch.bfloat16):
         y3 = lin(x)
     assert lin._weight_cache["q"] is not q1 and torch.equal(y3, fresh())
+
+
+@pytest.mark.parametrize("M,K,H", [(2048, 512, 2560), (256, 256, 384)])
+def test_fused_mlp_relu2_equals_the_unfused_chain(M, K, H):
+    """fusion.mlp_relu2 (ReLU^2 + abs-max in the first GEMM's epilogue, the ReLU^2 gradient in
+    the second linear's dgrad epilogue) is bit-identical to l2(relu2_abs_max(l1(x))), forward
+    and backward, with the same random draws -- on shapes the 2-SM kernel takes (first case)
+    and on shapes that use the GEMM + separate-kernel path (second)."""
+    from cloverlm_b200.fusion import mlp_relu2, relu2_abs_max
+    torch.manual_seed(9)
+    l1 = Quartet_II_linear(K, H, bias=False, device="cuda")
+    l2 = Quartet_II_linear(H, K, bias=False, device="cuda")
+    x = torch.randn(1, M, K, device="cuda")
+    grads = []
+    for fused in (True, False):
+        xi = x.clone().requires_grad_()
+        for m in (l1, l2):
+            m.weight.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                z = mlp_relu2(xi, l1, l2)
+            else:
+                h, amax = relu2_abs_max(l1(xi))
+                z = l2(h, input_abs_max=amax)
+        torch.manual_seed(21)
+        z.float().pow(2).mean().backward()
+        grads.append((z.detach(), xi.grad, l1.weight.grad.clone(), l2.weight.grad.clone()))
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)

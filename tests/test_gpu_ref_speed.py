@@ -124,3 +124,52 @@ def test_reference_gpu_path_vs_ours():
     print(f"step ms: reference {tot['ref']:.2f} ({flop / tot['ref'] / 1e9:.0f} TFLOP/s), "
           f"ours {tot['ours']:.2f} ({flop / tot['ours'] / 1e9:.0f} TFLOP/s)")
     assert tot["ours"] < 1.5 * tot["ref"]
+
+
+def test_gemm_per_shape_against_cudnn():
+    """Per-GEMM timing of ours against FlashInfer's cuDNN NVFP4 GEMM (the reference's _fp4_mm)
+    on the forward, dgrad and wgrad GEMMs of the 4B linear shapes, L2 evicted before every call
+    (run with -s for the table).  Asserts that both ran and that the set is within 15 % of cuDNN."""
+    mm_fp4 = pytest.importorskip("flashinfer").mm_fp4
+    from cloverlm_b200.linear import _fp4_mm
+    from cloverlm_b200.quant import NVFP4QuantMode, quant_fp4
+    M = int(os.environ.get("Q2B_REF_SPEED_TOKENS", "16384"))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def q(r, c, seed):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        return quant_fp4(torch.randn(r, c, device="cuda", generator=g).to(torch.bfloat16), scale_override=1.0,
+                         mode=NVFP4QuantMode.FOUR_SIX)
+
+    def timeit(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return sorted(ts)[len(ts) // 2]
+
+    tot = {"ours": 0.0, "cudnn": 0.0}
+    for name, K, N in SHAPES + [("kv", 3584, 896)]:
+        for kind, (m, n, k) in (("fwd", (M, N, K)), ("dgrad", (M, K, N)), ("wgrad", (N, K, M))):
+            A, B = q(m, k, 1), q(n, k, 2)
+            alpha = A.tensor_scale * B.tensor_scale
+            out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            t_o = timeit(lambda: _fp4_mm(A.fp4, B.fp4, A.micro_scales, B.micro_scales, alpha))
+            t_c = timeit(lambda: mm_fp4(A.fp4, B.fp4.T, A.micro_scales.view(torch.float8_e4m3fn).view(-1, k // 16),
+                                        B.micro_scales.view(torch.float8_e4m3fn).view(-1, k // 16).T, alpha,
+                                        torch.bfloat16, out, block_size=16, use_8x4_sf_layout=False,
+                                        backend="cudnn", use_nvfp4=True))
+            if name != "kv":
+                tot["ours"] += t_o
+                tot["cudnn"] += t_c
+            print(f"\n{name:8s} {kind:5s} {m}x{n}x{k}: ours {t_o:.3f} ms, cuDNN {t_c:.3f} ms, "
+                  f"cuDNN/ours {t_c / t_o:.2f}")
+    print(f"\nfused-QKV set at {M} tokens: ours {tot['ours']:.2f} ms, cuDNN {tot['cudnn']:.2f} ms")
+    assert tot["ours"] < 1.15 * tot["cudnn"]
