@@ -151,10 +151,19 @@ int launch_sr(void* sf, float* ts, const void* scratch, const unsigned* maxp, fl
   const int64_t n8 = nscales / 8;
   const int64_t want = (n8 + 255) / 256;
   const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
-  q2b::sr_scales_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<uint2*>(sf), ts,
-                                                 reinterpret_cast<const uint4*>(scratch), maxp, 1.f / fp8_max, seed,
-                                                 n8);
-  Q2B_CUDA(cudaGetLastError());
+  // programmatic dependent launch: scheduled as the EDEN kernel drains, the kernel waits
+  // (griddepcontrol.wait) for its results before reading them
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Q2B_CUDA(cudaLaunchKernelEx(&cfg, q2b::sr_scales_kernel, reinterpret_cast<uint2*>(sf), ts,
+                              reinterpret_cast<const uint4*>(scratch), maxp, 1.f / fp8_max, seed, n8));
   return Q2B_OK;
 }
 

@@ -458,6 +458,9 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 #endif
   tc_fence_before();
   __syncthreads();
+  // this CTA's work is issued: the SR pass (a programmatic dependent launch) may be scheduled;
+  // its griddepcontrol.wait still orders it after every write of this grid
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == Cfg::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
@@ -524,6 +527,9 @@ __global__ void __launch_bounds__(256) sr_scales_kernel(uint2* __restrict__ sf, 
                                                         const uint4* __restrict__ scratch,
                                                         const unsigned* __restrict__ max_bits, float inv_fp8_max,
                                                         uint64_t seed, int64_t n8) {
+  // launched as a programmatic dependent of the EDEN kernel: the CTAs may start while its last
+  // CTAs finish, and wait here until its writes (scratch, max word) are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float gs;
   const float f = sr_factor(__uint_as_float(*max_bits), inv_fp8_max, &gs);
   if (blockIdx.x == 0 && threadIdx.x == 0) *ts_out = gs;

@@ -167,7 +167,7 @@ class _AddRMSNormAmax(torch.autograd.Function):
         dx = torch.empty_like(g32)
         dy = torch.empty_like(y)
         props = torch.cuda.get_device_properties(y.device)
-        parts = max(1, min(rows, 2 * props.multi_processor_count))
+        parts = max(1, min(rows, 8 * props.multi_processor_count))  # eight blocks per SM keep enough loads in flight
         dw_part = torch.empty(parts, d, dtype=torch.float32, device=y.device)
         with torch.cuda.device(y.device):
             _lib.call("q2b_rmsnorm_bwd", _lib.ptr(dx), _lib.ptr(dy), _lib.ptr(dw_part), parts, _lib.ptr(g32),
