@@ -47,9 +47,12 @@ KERNELS_PER_CALL = {"q2b_abs_max": 1, "q2b_quant_fwd": 1, "q2b_rht_eden": 2, "q2
                     "q2b_watchdog_poll": 0}
 
 
-# DRAM bytes (read + write) per NVFP4 GEMM launch of the training step, from an ncu capture
-# (profiles/); None until one is summarised.
-GEMM_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) of one pair-GEMM launch of the training step's shapes, from the ncu
+# capture summarised in profiles/gemm_nvfp4_2sm_fwd_mlp_down_32k.txt (MLP-down forward, M=32768
+# N=3584 K=14336): 551.5 MB against 528.1 MB algorithmic (1.04x).
+GEMM_TRAFFIC_PER_LAUNCH = 551.5e6
+GEMM_TRAFFIC_NOTE = ("dram read+write of one MLP-down forward launch (M=32768, N=3584, K=14336) under ncu; "
+                     "algorithmic 528.1 MB, ratio 1.04")
 
 
 def load_peaks() -> dict:
@@ -135,35 +138,36 @@ class Instrument:
         self.gemm = []  # (start event, end event, flop, pair kernel?)
         self._lib, self._L, self._fusion = _lib, L, fusion
         self._orig_call = _lib.call
-        self._orig_mm = L._fp4_mm
-        self._orig_mm32 = L._fp4_mm_f32
         _lib.call = self._call
-        L._fp4_mm = self._mm
-        L._fp4_mm_f32 = self._mm32
-        fusion._fp4_mm = self._mm
+        # every NVFP4 GEMM wrapper of the training step, wherever it is referenced
+        for mod, name in ((L, "_fp4_mm"), (L, "_fp4_mm_f32"), (L, "_fp4_mm_relu2_bwd"), (L, "_fp4_mm_add"),
+                          (L, "_fp4_mm_relu2"), (fusion, "_fp4_mm"), (fusion, "_fp4_mm_relu2")):
+            setattr(mod, name, self._wrap(getattr(mod, name), name))
 
     def _call(self, name, *a):
         if self.active:
             self.launches += KERNELS_PER_CALL.get(name, 0)
         return self._orig_call(name, *a)
 
-    def _mm(self, a_fp4, b_fp4, a_sf, b_sf, alpha):
-        return self._timed(self._orig_mm, a_fp4, b_fp4, a_sf, b_sf, alpha)
+    def _wrap(self, fn, name):
+        if getattr(fn, "_bench_wrapped", False):
+            return fn
+        codes = 1 if name == "_fp4_mm_add" else 0  # position of A's codes (the add form takes out first)
 
-    def _mm32(self, a_fp4, b_fp4, a_sf, b_sf, alpha):
-        return self._timed(self._orig_mm32, a_fp4, b_fp4, a_sf, b_sf, alpha)
-
-    def _timed(self, fn, a_fp4, b_fp4, a_sf, b_sf, alpha):
-        if not self.active:
-            return fn(a_fp4, b_fp4, a_sf, b_sf, alpha)
-        torch = self.torch
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        out = fn(a_fp4, b_fp4, a_sf, b_sf, alpha)
-        e.record()
-        m, n, k = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
-        self.gemm.append((s, e, 2.0 * m * n * k, m % 256 == 0 and n % 256 == 0))
-        return out
+        def timed(*args, **kw):
+            if not self.active:
+                return fn(*args, **kw)
+            torch = self.torch
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*args, **kw)
+            e.record()
+            a_fp4, b_fp4 = args[codes], args[codes + 1]
+            m, n, k = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+            self.gemm.append((s, e, 2.0 * m * n * k, m % 256 == 0 and n % 256 == 0))
+            return out
+        timed._bench_wrapped = True
+        return timed
 
     def reset(self):
         self.launches = 0
@@ -425,6 +429,7 @@ def run_ours(args) -> None:
                                                   "shapes, gemm_nvfp4_kernel otherwise) inside the training step",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak if achieved else None, "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                     "traffic_note": GEMM_TRAFFIC_NOTE,
                      "peak_note": ("FP4 tensor-pipe ceiling measured in this run by q2b_fp4_mma_peak"
                                    if fp4_peak else "4 x measured sustained bf16 (MEASURED_PEAKS.json)"),
                      "frac_of_4x_bf16_sustained": achieved / (4.0 * peaks["bf16_tflops_sustained"]) if achieved
@@ -613,6 +618,65 @@ def small_m_report(dev, reps: int = 200) -> dict:
     return out
 
 
+KERNEL_CASES = {
+    # name: (what, shape) -- single-kernel workloads of the training step's shapes, for ncu captures
+    "gemm_fwd": "q2b_gemm_nvfp4 (pair kernel, bf16 out): MLP-down forward, M=32768 N=3584 K=14336",
+    "gemm_wgrad": "q2b_gemm_nvfp4_f32 (pair kernel, fp32 out): MLP-up wgrad, M=14336 N=3584 K=32768",
+    "eden_dual": "q2b_rht_eden_dual: E [32768, 14336] -> E and E^T",
+    "requant": "q2b_rht_requant: NVFP4 X [32768, 14336] -> X^T",
+    "quant_fwd": "q2b_quant_fwd four-over-six: [32768, 14336]",
+}
+
+
+def kernel_case(name: str, reps: int = 3) -> None:
+    """Run one kernel of the training step `reps` times on its own (inputs > L2, a few GB on the
+    device): the workload an ncu capture of that kernel uses.  Prints the mean CUDA-event time."""
+    import torch
+
+    from cloverlm_b200 import _lib
+    from cloverlm_b200.linear import _fp4_mm, _fp4_mm_f32, get_hadamard_matrix
+    from cloverlm_b200.quant import NVFP4QuantMode, quant_fp4, rht128_quant_eden_dual, rht128_requant
+    torch.cuda.set_device(0)
+    _lib.load(build_if_missing=False)
+    g = torch.Generator(device="cuda").manual_seed(11)
+
+    def rnd(r, c):
+        return torch.randn(r, c, device="cuda", generator=g).to(torch.bfloat16)
+
+    def q(r, c):
+        return quant_fp4(rnd(r, c), scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+
+    h = get_hadamard_matrix(128, torch.bfloat16, "cuda")[:16].contiguous()
+    if name == "gemm_fwd":
+        a, b = q(32768, 14336), q(3584, 14336)
+        fn = lambda: _fp4_mm(a.fp4, b.fp4, a.micro_scales, b.micro_scales, a.tensor_scale * b.tensor_scale)
+    elif name == "gemm_wgrad":
+        a, b = q(14336, 32768), q(3584, 32768)
+        fn = lambda: _fp4_mm_f32(a.fp4, b.fp4, a.micro_scales, b.micro_scales, a.tensor_scale * b.tensor_scale)
+    elif name == "eden_dual":
+        x = rnd(32768, 14336)
+        fn = lambda: rht128_quant_eden_dual(h=h, x=x, seed=torch.tensor(1), seed_t=torch.tensor(2))
+    elif name == "requant":
+        xq = q(32768, 14336)
+        fn = lambda: rht128_requant(x=xq.fp4, x_group_scales=xq.micro_scales, x_tensor_scale=xq.tensor_scale, h=h,
+                                    seed=torch.tensor(3))
+    elif name == "quant_fwd":
+        x = rnd(32768, 14336)
+        fn = lambda: quant_fp4(x, scale_override=1.0, mode=NVFP4QuantMode.FOUR_SIX)
+    else:
+        raise SystemExit(f"unknown kernel case {name!r}; choose from {sorted(KERNEL_CASES)}")
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    print(json.dumps({"kernel_case": name, "what": KERNEL_CASES[name], "ms": e0.elapsed_time(e1) / reps}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -632,7 +696,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-small-m", action="store_true", help="skip the inference-linear latency section")
     ap.add_argument("--no-quant-sweep", action="store_true", help="skip the quantizer sweep section")
+    ap.add_argument("--kernel-case", dest="kernel_case", choices=sorted(KERNEL_CASES),
+                    help="run one kernel of the training step on its own (for ncu captures) and exit")
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args.kernel_case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -522,7 +522,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   uint64_t* tfull = sfready + Cfg::kStages;
   uint64_t* tempty = tfull + 1;
   uint64_t* drain = tempty + 1;  // leader's tcgen05 issuers' final commits: nothing in flight at dealloc
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* auxbar = drain + 1;  // kEpiRelu2Bwd: one per epilogue warp, its TMA load of the a box
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(auxbar + Cfg::kEpiWarps);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #ifdef Q2B_GEMM2_STATS
@@ -546,6 +547,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * Cfg::kEpiWarps);
     mbar_init(drain, 1 + Cfg::kSfWarps);
+    for (int w = 0; w < Cfg::kEpiWarps; ++w) mbar_init(&auxbar[w], 1);
     fence_barrier_init();
   }
   if (threadIdx.x == 32) {
@@ -703,6 +705,7 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
     uint8_t* stage = smem + Cfg::kStagingOff + e * Cfg::kStagingPerWarp;
     float relu2_max = 0.f;
+    uint32_t aux_phase = 0;
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
       // tile coordinates before the wait: the drain is on the MMA's critical path
@@ -762,11 +765,19 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
             o[k] = pack_bf16x2(__uint_as_float(r[bx][2 * k]) * alpha, __uint_as_float(r[bx][2 * k + 1]) * alpha);
         }
         if constexpr (kEpi == kEpiRelu2Bwd) {
-          // da = 2 * relu(a) * g, g the bf16 dgrad value, a this lane's row of the pre-activation
-          const uint4* ap = reinterpret_cast<const uint4*>(p.aux + static_cast<int64_t>(row0 + lane) * p.N + col);
+          // da = 2 * relu(a) * g, g the bf16 dgrad value: the a box comes into this warp's
+          // staging buffer by TMA (once the previous store has read it), in the store's layout
+          if (lane == 0) {
+            bulk_wait_group_read0();
+            mbar_arrive_expect_tx(&auxbar[e], 32 * 64);
+            tma_load_2d(stage, &tmap_d2, &auxbar[e], col, row0);
+          }
+          __syncwarp();
+          if (!mbar_wait(&auxbar[e], aux_phase, kTimeoutTmaFull)) break;
+          aux_phase ^= 1u;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint4 av = __ldg(ap + k);
+            const uint4 av = *reinterpret_cast<const uint4*>(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
             const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {

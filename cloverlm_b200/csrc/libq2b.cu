@@ -778,6 +778,10 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     if (epi == q2b::kEpiRelu2) {
       if (int r = make_tmap(&td2, D2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
         return r;
+    } else if (epi == q2b::kEpiRelu2Bwd) {
+      // the pre-activation, loaded box by box in the store's layout
+      if (int r = make_tmap(&td2, aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return r;
     } else {
       td2 = td;
     }
