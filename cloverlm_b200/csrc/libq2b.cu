@@ -709,9 +709,11 @@ int q2b_rht_requant(void* codes, void* sf, float* ts, void* scratch, unsigned* s
   p.scratch_c = static_cast<uint16_t*>(scratch);
   p.max_c = scratch_max;
   Q2B_CUDA(cudaMemsetAsync(scratch_max, 0, sizeof(unsigned), st));
-  CUtensorMap unused;
-  std::memset(&unused, 0, sizeof(unused));
-  if (int r = launch_rht<q2b::kInFp4, q2b::kOutCols>(unused, p, sms, st)) return r;
+  CUtensorMap tmap;  // the codes, [M, N/2] bytes, 64-byte x 128-row boxes
+  if (int r = make_tmap(&tmap, x_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N / 2, M, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_NONE))
+    return r;
+  if (int r = launch_rht<q2b::kInFp4, q2b::kOutCols>(tmap, p, sms, st)) return r;
   return launch_sr(sf, ts, scratch, scratch_max, fp8_max, seed, M * N / 16, sms, st);
 }
 

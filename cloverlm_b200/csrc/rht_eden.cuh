@@ -66,22 +66,34 @@ constexpr uint32_t kHalfBytes = 128 * 128;      // one 64-column half of a tile
 template <int kIn, int kOut>
 struct RhtCfg {
   static constexpr int kNumOut = (kOut == kOutBoth) ? 2 : 1;
-  static constexpr int kProdWarps = (kIn == kInBf16) ? 1 : 8;
+  // NVFP4 input: one loader warp streams the codes (TMA) and scales (bulk
+  // copy) of each tile into a shared-memory ring; eight converter warps
+  // dequantize them into the bf16 tile.  bf16 input: one TMA warp.
+  static constexpr int kConvWarps = (kIn == kInBf16) ? 0 : 8;
+  static constexpr int kProdWarps = kConvWarps + 1;
+  static constexpr int kLoadWarp = kConvWarps;  // the last producer warp issues the loads
   static constexpr int kMmaWarp = kProdWarps;
   static constexpr int kEpiWarp0 = kProdWarps + 1;
-  // Groups of 4 epilogue warps (one per TMEM lane quarter) take tiles in turn,
-  // group g draining TMEM buffer g: two groups per orientation for the dual
-  // output (2 buffers x 256 columns), four for one orientation (4 x 128).
-  static constexpr int kEpiGroups = (kNumOut == 2) ? 2 : 4;
+  // TMEM buffers, taken by tiles in turn: two for the dual output (2 x 256
+  // columns), four for one orientation (4 x 128).  Groups of 4 epilogue warps
+  // (one per TMEM lane quarter, per orientation) take tiles in turn too; the
+  // number of groups divides the number of buffers.
+  static constexpr int kTmemBufs = (kNumOut == 2) ? 2 : 4;
   static constexpr int kEpiWarps = 16;
+  static constexpr int kEpiGroups = kEpiWarps / (4 * kNumOut);
+  static_assert(kTmemBufs % kEpiGroups == 0, "groups must divide buffers");
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
   static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
-  static constexpr uint32_t kTmemCols = kEpiGroups * kColsPerBuf;  // 512
-  // columns per TMEM round trip of an epilogue warp: 32 keeps the 800-thread
-  // requant block within 80 registers a thread
-  static constexpr int kChunkCols = (kIn == kInFp4) ? 32 : 64;
-  // shared memory: [H 32K][stages x 32K][barriers]
-  static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kRhtStages) + 256;
+  static constexpr uint32_t kTmemCols = kTmemBufs * kColsPerBuf;  // 512
+  // columns per TMEM load of a one-orientation epilogue warp, double-buffered:
+  // 16 keeps the 800-thread requant block within 80 registers a thread
+  static constexpr int kLdCols = (kIn == kInFp4) ? 16 : 32;
+  // NVFP4 input ring: per stage the tile's codes (128 rows x 64 bytes) and its
+  // two 512-byte blocks of scales
+  static constexpr int kRawStages = (kIn == kInFp4) ? 4 : 0;
+  static constexpr uint32_t kRawBytes = 128 * 64 + 1024;
+  // shared memory: [H 32K][stages x 32K][raw stages x 9K][barriers]
+  static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kRhtStages) + kRawStages * kRawBytes + 256;
 };
 
 // Byte offset of bf16 element (r, c) of a 128x128 tile stored as two 64-column
@@ -172,12 +184,15 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* hs = smem;
   uint8_t* tiles = smem + kTileBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + kRhtStages * kTileBytes);
+  uint8_t* raw = tiles + kRhtStages * kTileBytes;  // NVFP4 input ring
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw + Cfg::kRawStages * Cfg::kRawBytes);
   uint64_t* empty = full + kRhtStages;
   uint64_t* tfull = empty + kRhtStages;
   uint64_t* tempty = tfull + 4;
   uint64_t* drain = tempty + 4;  // the MMA warp's final commit: no MMA in flight at dealloc
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rfull = drain + 1;  // NVFP4 input ring: codes + scales landed
+  uint64_t* rempty = rfull + 4;  //   ... and read by every converter thread
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rempty + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // tile indices stay below 2^31 (the launcher checks), so the per-tile
@@ -190,17 +205,21 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRhtStages; ++s) {
-      mbar_init(&full[s], kIn == kInBf16 ? 1 : 32 * Cfg::kProdWarps);
+      mbar_init(&full[s], kIn == kInBf16 ? 1 : 32 * Cfg::kConvWarps);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < Cfg::kEpiGroups; ++b) {
+    for (int s = 0; s < Cfg::kRawStages; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 32 * Cfg::kConvWarps);
+    }
+    for (int b = 0; b < Cfg::kTmemBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4 * Cfg::kNumOut);  // the group(s) of epilogue warps of this buffer
     }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
-  if (kIn == kInBf16 && threadIdx.x == 0) prefetch_tmap(&tmap_x);
+  if (threadIdx.x == 0) prefetch_tmap(&tmap_x);
   if (warp == Cfg::kMmaWarp) {
     tmem_alloc(tmem_holder, Cfg::kTmemCols);
     tmem_relinquish();
@@ -234,55 +253,67 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         for (int k = issued > kRhtStages ? issued - kRhtStages : 0; k < issued; ++k)
           mbar_wait(&full[k % kRhtStages], (k / kRhtStages) & 1, kTimeoutProducer);
       }
+    } else if (warp == Cfg::kLoadWarp) {
+      // NVFP4 input, loader: the tile's 128 x 64 code bytes by TMA and its two
+      // contiguous 512-byte scale blocks (blocked layout: 128 rows x 4 groups
+      // each) by one bulk copy, on one barrier
+      if (lane == 0) {
+        const int64_t n_kt = p.N >> 6;  // 4-group column blocks of the scales
+        int it = 0;
+        for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+          const int slot = it % Cfg::kRawStages;
+          const uint32_t ph = (it / Cfg::kRawStages) & 1;
+          if (!mbar_wait(&rempty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
+          const uint32_t t32 = static_cast<uint32_t>(t);
+          const int tm = static_cast<int>(t32 / tiles_n), tn = static_cast<int>(t32 % tiles_n);
+          uint8_t* dst = raw + slot * Cfg::kRawBytes;
+          mbar_arrive_expect_tx(&rfull[slot], Cfg::kRawBytes);
+          tma_load_2d(dst, &tmap_x, &rfull[slot], tn * 64, tm * 128);
+          bulk_load(dst + 128 * 64, p.x_sf + ((static_cast<int64_t>(tm) * n_kt + 2 * tn) << 9), 1024, &rfull[slot]);
+        }
+        const int issued = it;
+        for (int k = issued > Cfg::kRawStages ? issued - Cfg::kRawStages : 0; k < issued; ++k)
+          mbar_wait(&rfull[k % Cfg::kRawStages], (k / Cfg::kRawStages) & 1, kTimeoutProducer);
+      }
     } else {
-      // NVFP4 input: each producer thread dequantizes pairs of 16-element
-      // groups of the tile (16 code bytes + 2 scale bytes -> 64 bytes of bf16);
-      // four consecutive lanes cover one row's 64-byte code segment, so a
-      // warp's 16-byte loads are contiguous 64-byte runs of 8 rows.
-      const int pt = threadIdx.x;  // 0 .. 32*kProdWarps-1
+      // NVFP4 input, converters: each thread dequantizes pairs of 16-element
+      // groups of the tile (16 code bytes + 2 scale bytes -> 64 bytes of
+      // bf16) from the ring into the swizzled bf16 tile; four consecutive
+      // lanes cover one row's 64 code bytes, so a warp reads 512 contiguous
+      // bytes.
+      const int pt = threadIdx.x;  // 0 .. 32*kConvWarps-1
       const float x_ts = *p.x_ts;
-      const int64_t n_kblk = p.N >> 4, n_kt = n_kblk >> 2;
-      constexpr int kItems = 128 * 4 / (32 * Cfg::kProdWarps);  // (row, group pair) items per thread
-      // registers hold the codes and scales of the next TWO tiles while this
-      // tile is converted, so two tiles of conversion hide each global load
-      uint4 qa[kItems], qb[kItems];
-      uint32_t sa[kItems], sbb[kItems];
-      auto load_tile = [&](int64_t t, uint4 (&q)[kItems], uint32_t (&sb)[kItems]) {
-        const uint32_t t32 = static_cast<uint32_t>(t);
-        const int64_t tm = t32 / tiles_n, tn = t32 % tiles_n;
+      constexpr int kItems = 128 * 4 / (32 * Cfg::kConvWarps);  // (row, group pair) items per thread
+      int it = 0;
+      Q2B_R_T(_pl)
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int rs = it % Cfg::kRawStages;
+        Q2B_R_T(_p0)
+        if (!mbar_wait(&rfull[rs], (it / Cfg::kRawStages) & 1, kTimeoutTmaFull)) break;
+        Q2B_R_ADD(9, clock64() - _p0)
+        const uint8_t* src = raw + rs * Cfg::kRawBytes;
+        uint4 qc[kItems];
+        uint32_t sc[kItems];
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
-          const int item = pt + u * 32 * Cfg::kProdWarps;
+          const int item = pt + u * 32 * Cfg::kConvWarps;
           const int r = item >> 2, gp = item & 3;  // row, pair of 16-col groups of the tile
-          const int64_t row = tm * 128 + r;
-          q[u] = __ldcs(reinterpret_cast<const uint4*>(p.x_codes + row * (p.N >> 1) + tn * 64 + gp * 16));
-          const int64_t kb = tn * 8 + 2 * gp;  // even: the pair's two scale bytes are adjacent
-          const int64_t so = (((row >> 7) * n_kt + (kb >> 2)) << 9) | ((row & 31) << 4) | (((row >> 5) & 3) << 2) |
-                             (kb & 3);
-          sb[u] = *reinterpret_cast<const uint16_t*>(p.x_sf + so);
+          qc[u] = *reinterpret_cast<const uint4*>(src + r * 64 + gp * 16);
+          const int kb = 2 * gp;  // even: the pair's two scale bytes are adjacent
+          sc[u] = *reinterpret_cast<const uint16_t*>(src + 128 * 64 + (((kb >> 2) << 9) | ((r & 31) << 4) |
+                                                                       (((r >> 5) & 3) << 2) | (kb & 3)));
         }
-      };
-      auto convert = [&](int it, const uint4 (&qc)[kItems], const uint32_t (&sc)[kItems]) -> bool {
+        mbar_arrive(&rempty[rs]);
         const int slot = it % kRhtStages;
         const uint32_t ph = (it / kRhtStages) & 1;
-        Q2B_R_T(_p0)
-        if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) return false;
         Q2B_R_T(_p1)
-        Q2B_R_ADD(0, _p1 - _p0)
-#ifdef Q2B_RHT_STATS
-        {  // time until this tile's prefetched codes are in registers
-          uint32_t dep = 0;
-#pragma unroll
-          for (int u = 0; u < kItems; ++u) dep ^= qc[u].x ^ qc[u].w ^ sc[u];
-          asm volatile("" ::"r"(dep));
-          if (dep == 0x9e3779b9u) q2b_rs[11] += 1;
-          Q2B_R_ADD(9, clock64() - _p1)
-        }
-#endif
+        if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
+        Q2B_R_T(_p2)
+        Q2B_R_ADD(0, _p2 - _p1)
         uint8_t* dst = tiles + slot * kTileBytes;
 #pragma unroll
         for (int u = 0; u < kItems; ++u) {
-          const int item = pt + u * 32 * Cfg::kProdWarps;
+          const int item = pt + u * 32 * Cfg::kConvWarps;
           const int r = item >> 2, gp = item & 3;
 #pragma unroll
           for (int k = 0; k < 2; ++k) {  // the pair's two groups
@@ -304,31 +335,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&full[slot]);
-        Q2B_R_ADD(1, clock64() - _p1)
-        return true;
-      };
-      const int64_t step = gridDim.x;
-      Q2B_R_T(_pl)
-      int64_t t = blockIdx.x;
-      if (t < ntiles) load_tile(t, qa, sa);
-      if (t + step < ntiles) load_tile(t + step, qb, sbb);
-      int it = 0;
-      while (t < ntiles) {
-        uint4 qc[kItems];
-        uint32_t sc[kItems];
-#pragma unroll
-        for (int u = 0; u < kItems; ++u) { qc[u] = qa[u]; sc[u] = sa[u]; }
-        if (t + 2 * step < ntiles) load_tile(t + 2 * step, qa, sa);
-        if (!convert(it, qc, sc)) break;
-        t += step;
-        ++it;
-        if (t >= ntiles) break;
-#pragma unroll
-        for (int u = 0; u < kItems; ++u) { qc[u] = qb[u]; sc[u] = sbb[u]; }
-        if (t + 2 * step < ntiles) load_tile(t + 2 * step, qb, sbb);
-        if (!convert(it, qc, sc)) break;
-        t += step;
-        ++it;
+        Q2B_R_ADD(1, clock64() - _p2)
       }
       Q2B_R_ADD(2, clock64() - _pl)
     }
@@ -343,8 +350,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
       const int slot = it % kRhtStages;
       const uint32_t ph = (it / kRhtStages) & 1;
-      const int buf = it % Cfg::kEpiGroups;
-      const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
+      const int buf = it % Cfg::kTmemBufs;
+      const uint32_t bph = (it / Cfg::kTmemBufs) & 1;
       Q2B_R_T(_m0)
       ok = mbar_wait(&tempty[buf], bph ^ 1, kTimeoutTmemEmpty);
       Q2B_R_T(_m1)
@@ -385,9 +392,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     const int e = warp - Cfg::kEpiWarp0;   // 0 .. kEpiWarps-1
     const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int orient = (kOut == kOutBoth) ? (e >> 3) : (kOut == kOutRows ? 0 : 1);  // 0 rows, 1 cols
-    // Groups of epilogue warps take tiles in turn (group g owns TMEM buffer
-    // g), each warp draining its 32 rows x 128 columns in chunks: while one
-    // group waits for its TMEM loads the others compute.
+    // Groups of epilogue warps take tiles in turn (tile i is drained from
+    // TMEM buffer i % kTmemBufs), each warp draining its 32 rows x 128
+    // columns in chunks: while one group waits for its TMEM loads the others
+    // compute.
     const int grp = (e >> 2) % Cfg::kEpiGroups;
     const uint32_t col_base = (kOut == kOutBoth && orient == 1) ? 128 : 0;
     uint8_t* codes = orient == 0 ? p.codes_r : p.codes_c;
@@ -395,14 +403,14 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     unsigned* maxp = orient == 0 ? p.max_r : p.max_c;
     const int64_t out_cols = orient == 0 ? p.N : p.M;  // length of an output row
     const int64_t n_kblk = out_cols >> 4, n_kt = n_kblk >> 2;
-    constexpr int kChunk = Cfg::kChunkCols, kNChunks = 128 / kChunk, kG = kChunk / 16;
+    constexpr int kLd = Cfg::kLdCols, kNLd = 128 / kLd;
     float run_max = 0.f;
     Q2B_R_T(_el)
     for (int it = grp;; it += Cfg::kEpiGroups) {
       const int64_t t = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
       if (t >= ntiles) break;
-      const int buf = grp;
-      const uint32_t bph = (it / Cfg::kEpiGroups) & 1;
+      const int buf = it % Cfg::kTmemBufs;
+      const uint32_t bph = (it / Cfg::kTmemBufs) & 1;
       Q2B_R_T(_w0)
       if (!mbar_wait(&tfull[buf], bph, kTimeoutTmemFull)) break;
       Q2B_R_ADD(7, clock64() - _w0)
@@ -412,35 +420,73 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       const int64_t orow = (orient == 0 ? tm : tn) * 128 + q * 32 + lane;
       const int64_t ogrp = orient == 0 ? tn : tm;  // 128-group index along the output row
       const uint32_t taddr0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::kColsPerBuf + col_base;
+      if constexpr (Cfg::kNumOut == 2) {
+        // dual output: two TMEM buffers only, so the hand-off comes first --
+        // two 64-column round trips, the buffer released after the second load
+        constexpr int kChunk = 64, kNChunks = 2, kG = 4;
 #pragma unroll
-      for (int ch = 0; ch < kNChunks; ++ch) {
-        uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + ch * (kChunk / 2);
-        const uint32_t taddr = taddr0 + ch * kChunk;
-        uint32_t r[kChunk / 32][32];
+        for (int ch = 0; ch < kNChunks; ++ch) {
+          uint8_t* crow = codes + orow * (out_cols >> 1) + ogrp * 64 + ch * (kChunk / 2);
+          const uint32_t taddr = taddr0 + ch * kChunk;
+          uint32_t r[kChunk / 32][32];
 #pragma unroll
-        for (int h = 0; h < kChunk / 32; ++h) tmem_ld_32x32b_x32(taddr + 32 * h, r[h]);
-        Q2B_R_T(_l1)
-        tmem_ld_wait();
-        Q2B_R_ADD(8, clock64() - _l1)
-        if (ch == kNChunks - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
-        }
-        uint32_t cw[2 * kG], fs[kG];
+          for (int h = 0; h < kChunk / 32; ++h) tmem_ld_32x32b_x32(taddr + 32 * h, r[h]);
+          Q2B_R_T(_l1)
+          tmem_ld_wait();
+          Q2B_R_ADD(8, clock64() - _l1)
+          if (ch == kNChunks - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
+          }
+          uint32_t cw[2 * kG], fs[kG];
 #pragma unroll
-        for (int g = 0; g < kG; ++g)
-          run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
+          for (int g = 0; g < kG; ++g)
+            run_max = fmaxf(run_max, eden16(r[g >> 1] + 16 * (g & 1), p.inv_fp4_max, cw[2 * g], cw[2 * g + 1], fs[g]));
 #pragma unroll
-        for (int v = 0; v < kG / 2; ++v)
-          __stcs(reinterpret_cast<uint4*>(crow + 16 * v), make_uint4(cw[4 * v], cw[4 * v + 1], cw[4 * v + 2], cw[4 * v + 3]));
-        const int64_t kb = ogrp * 8 + ch * kG;
-        const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2) |
-                           (kb & 3);
-        if constexpr (kG == 4)
+          for (int v = 0; v < kG / 2; ++v)
+            __stcs(reinterpret_cast<uint4*>(crow + 16 * v), make_uint4(cw[4 * v], cw[4 * v + 1], cw[4 * v + 2], cw[4 * v + 3]));
+          const int64_t kb = ogrp * 8 + ch * kG;
+          const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) | (((orow >> 5) & 3) << 2) |
+                             (kb & 3);
           *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
-        else
-          *reinterpret_cast<uint32_t*>(scratch + so) = fs[0] | (fs[1] << 16);
+        }
+      } else {
+        // one orientation (four TMEM buffers): loads run one chunk ahead of
+        // the EDEN arithmetic (two register buffers), so only the first load
+        // of a tile is exposed
+        uint32_t r[2][kLd];
+        uint32_t cw[4], fs[4];
+        tmem_ld_cols<kLd>(taddr0, r[0]);
+        Q2B_R_T(_l1)
+        tmem_ld_wait_regs<kLd>(r[0]);
+        Q2B_R_ADD(8, clock64() - _l1)
+#pragma unroll
+        for (int l = 0; l < kNLd; ++l) {
+          if (l + 1 < kNLd) {
+            tmem_ld_cols<kLd>(taddr0 + (l + 1) * kLd, r[(l + 1) & 1]);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_relaxed(&tempty[buf]);  // TMEM hand-off only
+          }
+#pragma unroll
+          for (int gg = 0; gg < kLd / 16; ++gg) {
+            const int g = l * (kLd / 16) + gg;  // 16-column group of the tile's row
+            run_max = fmaxf(run_max, eden16(r[l & 1] + 16 * gg, p.inv_fp4_max, cw[2 * (g & 1)], cw[2 * (g & 1) + 1],
+                                            fs[g & 3]));
+            if ((g & 1) == 1)
+              __stcs(reinterpret_cast<uint4*>(codes + orow * (out_cols >> 1) + ogrp * 64 + (g >> 1) * 16),
+                     make_uint4(cw[0], cw[1], cw[2], cw[3]));
+            if ((g & 3) == 3) {
+              const int64_t kb = ogrp * 8 + (g - 3);
+              const int64_t so = (((orow >> 7) * n_kt + (kb >> 2)) << 9) | ((orow & 31) << 4) |
+                                 (((orow >> 5) & 3) << 2) | (kb & 3);
+              *reinterpret_cast<uint2*>(scratch + so) = make_uint2(fs[0] | (fs[1] << 16), fs[2] | (fs[3] << 16));
+            }
+          }
+          if (l + 1 < kNLd) tmem_ld_wait_regs<kLd>(r[(l + 1) & 1]);
+        }
       }
     }
     Q2B_R_ADD(10, clock64() - _el)
