@@ -343,7 +343,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     // ------------------------------------------------------------ MMA issue
     const uint32_t id_rows = idesc_bf16(128, 128, false, false);
     const uint32_t id_cols = idesc_bf16(128, 128, true, false);
-    const uint32_t hs_addr = smem_u32(hs);
+    const bool lead = lane == 0;
+    const uint64_t h_desc0 = smem_desc(smem_u32(hs), 0, 1024, kLayoutSW128);
+    const uint64_t rows_desc0 = smem_desc(smem_u32(tiles), 0, 1024, kLayoutSW128);
+    const uint64_t cols_desc0 = smem_desc(smem_u32(tiles), kHalfBytes, 1024, kLayoutSW128);
     int it = 0;
     bool ok = true;
     Q2B_R_T(_ml)
@@ -361,24 +364,23 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
       Q2B_R_ADD(6, 1)
       if (!ok) break;
       tc_fence_after();
-      if (lane == 0) {
-        const uint32_t a_addr = smem_u32(tiles + slot * kTileBytes);
-        const uint32_t d = tmem + buf * Cfg::kColsPerBuf;
+      // converged warp, one lane issuing through a predicate; descriptors are
+      // the per-CTA bases plus compile-time offsets (start address >> 4 in
+      // the low bits)
+      const uint64_t slot_off = (slot * kTileBytes) >> 4;
+      const uint32_t d = tmem + buf * Cfg::kColsPerBuf;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const uint64_t bdesc = smem_desc(hs_addr + (s >> 2) * kHalfBytes + (s & 3) * 32, 0, 1024, kLayoutSW128);
-          if constexpr ((kOut & kOutRows) != 0) {
-            const uint64_t adesc = smem_desc(a_addr + (s >> 2) * kHalfBytes + (s & 3) * 32, 0, 1024, kLayoutSW128);
-            umma_bf16(d, adesc, bdesc, id_rows, s > 0);
-          }
-          if constexpr ((kOut & kOutCols) != 0) {
-            const uint64_t adesc = smem_desc(a_addr + s * 2048, kHalfBytes, 1024, kLayoutSW128);
-            umma_bf16(d + ((kOut & kOutRows) ? 128 : 0), adesc, bdesc, id_cols, s > 0);
-          }
-        }
-        tc_commit(&empty[slot]);
-        tc_commit(&tfull[buf]);
+      for (int s = 0; s < 8; ++s) {
+        const uint64_t bdesc = h_desc0 + (((s >> 2) * kHalfBytes + (s & 3) * 32) >> 4);
+        if constexpr ((kOut & kOutRows) != 0)
+          umma_bf16_if(lead, d, rows_desc0 + slot_off + (((s >> 2) * kHalfBytes + (s & 3) * 32) >> 4), bdesc,
+                       id_rows, s > 0);
+        if constexpr ((kOut & kOutCols) != 0)
+          umma_bf16_if(lead, d + ((kOut & kOutRows) ? 128 : 0), cols_desc0 + slot_off + ((s * 2048) >> 4), bdesc,
+                       id_cols, s > 0);
       }
+      tc_commit_if(lead, &empty[slot]);
+      tc_commit_if(lead, &tfull[buf]);
       __syncwarp();
     }
     Q2B_R_ADD(5, clock64() - _ml)
