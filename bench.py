@@ -264,6 +264,19 @@ def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument
     if world > 1:
         comm = GradAllReduce(list(model.parameters()), mode="overlap", bucket_mb=args.bucket_mb, copy_back=False)
     step = TrainStep(model, opt, comm)
+    # exposed exchange: device time the compute stream stalls in comm.wait() (the last buckets'
+    # all-reduces that the backward did not hide), CUDA events around the wait on that stream
+    waits = []
+    if comm is not None:
+        inner_wait = comm.wait
+
+        def timed_wait():
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            inner_wait()
+            b.record()
+            waits.append((a, b))
+        comm.wait = timed_wait
     gen = torch.Generator(device=dev).manual_seed(654356 + rank * 2097593)  # per-rank data (utils_data.py:266-269)
     shape = (args.accum, args.micro_batch, cfg.context + 1)
     pool = [torch.randint(0, cfg.vocab_size, shape, device=dev, generator=gen) for _ in range(4)]
@@ -283,6 +296,7 @@ def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument
     time.sleep(0.3)
     inst.reset()
     inst.active = True
+    waits.clear()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for i in range(args.steps):
@@ -296,6 +310,7 @@ def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument
     clocks = sampler.stop()
     losses.append(loss.item())
     ms = ev0.elapsed_time(ev1) / args.steps
+    exposed_ms = sum(a.elapsed_time(b) for a, b in waits) / args.steps if waits else 0.0
     gemm = inst.gemm_summary(args.steps)
     launches = inst.launches // args.steps
     mem = torch.cuda.max_memory_allocated(dev)
@@ -322,9 +337,9 @@ def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, exposed_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
+        ms, e2e_ms, exposed_ms = t.tolist()
     tokens = args.accum * args.micro_batch * cfg.context
     out = {
         "ms_per_step": ms, "tokens_per_gpu": tokens, "value": world * tokens / (ms / 1e3),
@@ -337,6 +352,13 @@ def train_measure(args, world: int, rank: int, local: int, dev, inst: Instrument
         "loss_first_last": [losses[0], losses[-1]], "max_memory_gb": mem / 1e9,
         "params": sum(p.numel() for p in model.parameters()),
     }
+    if comm is not None:
+        nbytes = sum(f.numel() * f.element_size() for f in comm._flat if f is not None)
+        out["exchange"] = {"bytes_per_gpu": nbytes, "buckets": len(comm.buckets),
+                           "exposed_ms_per_step": exposed_ms, "exposed_share_of_step": exposed_ms / ms,
+                           "note": "device time the compute stream waits in GradAllReduce.wait() per step "
+                                   "(CUDA events on that stream, max over ranks); the rest of the all-reduce "
+                                   "time overlaps the last backward"}
     if comm is not None:
         comm.close()
     del model, opt, comm, step, pool
@@ -375,6 +397,7 @@ def linear_set_measure(dev, tokens: int, steps: int, warmup: int, inst: Instrume
     torch.cuda.synchronize()
     inst.reset()
     inst.active = True
+    waits.clear()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(steps):
@@ -412,7 +435,11 @@ def run_ours(args) -> None:
     tr = train_measure(args, world, rank, local, dev, inst)
     peaks = load_peaks()
     cfg = CloverLMConfig()
-    fp4_peak = fp4_mma_peak_report(dev) if world == 1 else None
+    fp4_peak = fp4_mma_peak_report(dev)
+    if world > 1:  # the slowest rank's ceiling
+        t = torch.tensor([fp4_peak["tflops"]], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        fp4_peak["tflops"] = t.item()
     peak = fp4_peak["tflops"] if fp4_peak else 4.0 * peaks["bf16_tflops_sustained"]
     achieved = tr["gemm"]["tflops"]
     line = {
@@ -438,7 +465,7 @@ def run_ours(args) -> None:
         "gpu_launches": tr["gpu_launches"],
         "clocks": tr["clocks"],
         "train": {k: tr[k] for k in ("model_tflops", "linear_tflops", "gemm", "loss_first_last", "max_memory_gb",
-                                     "params")},
+                                     "params", "exchange") if k in tr},
         "lib": _lib.lib_path(),
     }
     if fp4_peak:

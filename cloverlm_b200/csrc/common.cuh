@@ -346,6 +346,24 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
 // Two fp32 -> packed E2M1 byte (as in cvt_e2m1x2) and, from the same byte
 // register, its two decoded values as fp16x2 -- one asm block, so the byte
 // never round-trips through a 32-bit register between the conversions.
+// Eight values -> one word of E2M1 codes (value 2j in the low nibble of byte
+// j, round-to-nearest-even, saturating) and the four f16x2 pairs the codes
+// decode to; the code bytes are packed in registers, with no byte extraction.
+__device__ __forceinline__ void cvt_e2m1x8_back(const float (&v)[8], uint32_t& word, uint32_t (&back)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %8, %7;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %10, %9;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %12, %11;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %4, b3;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(word), "=r"(back[0]), "=r"(back[1]), "=r"(back[2]), "=r"(back[3])
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+}
+
 __device__ __forceinline__ void cvt_e2m1x2_back(float lo, float hi, uint32_t& byte, uint32_t& back_h2) {
   asm("{\n\t.reg .b8 b;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b, %2, %3;\n\t"

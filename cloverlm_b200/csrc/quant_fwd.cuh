@@ -22,6 +22,22 @@ namespace q2b {
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Abs-max of a group's 16 bf16 values (eight packed words): a tree of packed
+// max(|a|, |b|) (the result's sign is the xor of the inputs' and is dropped at
+// the end), exact and order-independent like any maximum.
+__device__ __forceinline__ uint32_t maxabs_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ float group_absmax16(const uint32_t (&w)[8]) {
+  const uint32_t m = maxabs_bf16x2(maxabs_bf16x2(maxabs_bf16x2(w[0], w[1]), maxabs_bf16x2(w[2], w[3])),
+                                   maxabs_bf16x2(maxabs_bf16x2(w[4], w[5]), maxabs_bf16x2(w[6], w[7]))) &
+                     0x7FFF7FFFu;
+  return fmaxf(bf16lo(m), bf16hi(m));
+}
+
 // Per-tensor lookup tables indexed by the E4M3 scale byte (0..127):
 //   factor[s8]  = 1 / (s8' * ts)   (s8' = 1 when s8 == 0)
 //   descale[s8] = e4m3(s8) * ts    (0 stays 0)
@@ -57,14 +73,19 @@ __device__ __forceinline__ float quant16(const float (&xs)[16], float gabs, floa
   s8 = cvt_e4m3(gabs * inv_c * inv_ts);
   const float f = tab.factor[s8];
   const float nd = -tab.descale[s8];
-  uint32_t b[8], h[8];
+  uint32_t h[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float2 w = fmul2(make_float2(xs[2 * k], xs[2 * k + 1]), make_float2(f, f));
-    cvt_e2m1x2_back(w.x, w.y, b[k], h[k]);
+  for (int hw = 0; hw < 2; ++hw) {  // 8 values -> one code word
+    float w[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 p = fmul2(make_float2(xs[8 * hw + 2 * k], xs[8 * hw + 2 * k + 1]), make_float2(f, f));
+      w[2 * k] = p.x;
+      w[2 * k + 1] = p.y;
+    }
+    uint32_t (&hb)[4] = *reinterpret_cast<uint32_t (*)[4]>(h + 4 * hw);
+    cvt_e2m1x8_back(w, hw == 0 ? codes.x : codes.y, hb);
   }
-  codes.x = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
-  codes.y = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
   // signed errors: a code carries its input's sign (or is zero), so x - q*s is
   // exactly +-(|x| - |q|*s) (a fused multiply-add of negated inputs is the
   // negated exact result) and its square is the magnitude form's, bit for bit
@@ -110,18 +131,13 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
     const bool valid = g < ngroups;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
-    float xs[16], xa[16];
+    float xs[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       xs[2 * k] = bf16lo(w[k]);
       xs[2 * k + 1] = bf16hi(w[k]);
-      const uint32_t a = w[k] & 0x7FFF7FFFu;
-      xa[2 * k] = bf16lo(a);
-      xa[2 * k + 1] = bf16hi(a);
     }
-    // group abs-max with three-input maxima (exact, order-independent)
-    const float gabs = fmaxf(fmax3(fmax3(xa[0], xa[1], xa[2]), fmax3(xa[3], xa[4], xa[5]), fmax3(xa[6], xa[7], xa[8])),
-                             fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
+    const float gabs = group_absmax16(w);
     uint2 c;
     uint32_t s;
     const float e6 = quant16(xs, gabs, inv6, inv_ts, tab, c, s);
@@ -207,18 +223,13 @@ __global__ void __launch_bounds__(kRowsThreads) quant_rows_cluster_kernel(
     const bool valid = g < ngroups;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
-    float xs[16], xa[16];
+    float xs[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       xs[2 * k] = bf16lo(w[k]);
       xs[2 * k + 1] = bf16hi(w[k]);
-      const uint32_t a = w[k] & 0x7FFF7FFFu;
-      xa[2 * k] = bf16lo(a);
-      xa[2 * k + 1] = bf16hi(a);
     }
-    // group abs-max with three-input maxima (exact, order-independent)
-    const float gabs = fmaxf(fmax3(fmax3(xa[0], xa[1], xa[2]), fmax3(xa[3], xa[4], xa[5]), fmax3(xa[6], xa[7], xa[8])),
-                             fmax3(fmax3(xa[9], xa[10], xa[11]), fmax3(xa[12], xa[13], xa[14]), xa[15]));
+    const float gabs = group_absmax16(w);
     uint2 c;
     uint32_t sc;
     const float e6 = quant16(xs, gabs, inv6, inv_ts, tab, c, sc);

@@ -140,19 +140,27 @@ __device__ __forceinline__ float eden16(const uint32_t* r, float inv_fp4_max, ui
   float f;
   if (fabsf(m3) < FLT_MIN) { m3 = 0.f; f = 0.f; } else { f = rcp_approx_ftz(m3); }
   float2 xx = make_float2(0.f, 0.f), xy = make_float2(0.f, 0.f);
-  uint32_t b[8];
-#pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    const float2 w = fmul2(make_float2(__uint_as_float(r[2 * t]), __uint_as_float(r[2 * t + 1])), make_float2(f, f));
-    uint32_t h2;
-    cvt_e2m1x2_back(w.x, w.y, b[t], h2);
-    const float2 back = f16x2_to_f32x2(h2);
-    xx = ffma2(w, w, xx);
-    xy = ffma2(w, back, xy);
-  }
   uint32_t c[2];
-  c[0] = __byte_perm(__byte_perm(b[0], b[1], 0x1140), __byte_perm(b[2], b[3], 0x1140), 0x5410);
-  c[1] = __byte_perm(__byte_perm(b[4], b[5], 0x1140), __byte_perm(b[6], b[7], 0x1140), 0x5410);
+#pragma unroll
+  for (int hw = 0; hw < 2; ++hw) {  // 8 values -> one code word
+    float w[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 p = fmul2(make_float2(__uint_as_float(r[8 * hw + 2 * t]), __uint_as_float(r[8 * hw + 2 * t + 1])),
+                             make_float2(f, f));
+      w[2 * t] = p.x;
+      w[2 * t + 1] = p.y;
+    }
+    uint32_t h2[4];
+    cvt_e2m1x8_back(w, c[hw], h2);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 wv = make_float2(w[2 * t], w[2 * t + 1]);
+      const float2 back = f16x2_to_f32x2(h2[t]);
+      xx = ffma2(wv, wv, xx);
+      xy = ffma2(wv, back, xy);
+    }
+  }
   const float xx_t = xx.x + xx.y, xy_t = xy.x + xy.y;
   const float corr = (xy_t == 0.f) ? 1.f : xx_t * rcp_approx_ftz(xy_t);
   const float fixed = m3 * corr;
