@@ -374,6 +374,18 @@ __device__ __forceinline__ void cvt_e2m1x2_back(float lo, float hi, uint32_t& by
 }
 
 // Packed E2M1 byte -> two fp16 values (low nibble in the low half).
+// One word of eight E2M1 codes -> four f16x2 pairs (pair j from byte j).
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t word, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(word));
+}
+
 __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   uint32_t r;
   asm("{\n\t.reg .b8 b;\n\t"

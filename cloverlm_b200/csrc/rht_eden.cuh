@@ -79,7 +79,7 @@ struct RhtCfg {
   // (one per TMEM lane quarter, per orientation) take tiles in turn too; the
   // number of groups divides the number of buffers.
   static constexpr int kTmemBufs = (kNumOut == 2) ? 2 : 4;
-  static constexpr int kEpiWarps = 16;
+  static constexpr int kEpiWarps = (kIn == kInFp4) ? 24 - kConvWarps : 16;
   static constexpr int kEpiGroups = kEpiWarps / (4 * kNumOut);
   static_assert(kTmemBufs % kEpiGroups == 0, "groups must divide buffers");
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
@@ -330,10 +330,11 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 #pragma unroll
             for (int half = 0; half < 2; ++half) {  // 8 elements -> one 16-byte chunk
               const uint32_t w = k == 0 ? (half ? qc[u].y : qc[u].x) : (half ? qc[u].w : qc[u].z);
-              uint32_t o[4];
+              uint32_t o[4], hq[4];
+              e2m1x8_to_f16x2(w, hq);
 #pragma unroll
               for (int b = 0; b < 4; ++b) {
-                const float2 dq = f16x2_to_f32x2(e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu));
+                const float2 dq = f16x2_to_f32x2(hq[b]);
                 const float2 v = fmul2(dq, make_float2(gs, gs));
                 o[b] = pack_bf16x2(v.x, v.y);
               }
