@@ -397,7 +397,6 @@ def linear_set_measure(dev, tokens: int, steps: int, warmup: int, inst: Instrume
     torch.cuda.synchronize()
     inst.reset()
     inst.active = True
-    waits.clear()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(steps):

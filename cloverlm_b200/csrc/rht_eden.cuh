@@ -534,24 +534,41 @@ __device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint32_t ctr) {
   uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
 #pragma unroll
   for (int i = 0; i < 10; ++i) {
-    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
-    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
-    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
-    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    // one widening multiply gives both halves of each 32 x 32 -> 64 product
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c0;
+    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c2;
+    const uint32_t n0 = static_cast<uint32_t>(p1 >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = static_cast<uint32_t>(p0 >> 32) ^ c3 ^ k1;
+    c0 = n0; c1 = static_cast<uint32_t>(p1); c2 = n2; c3 = static_cast<uint32_t>(p0);
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;
   }
   return make_uint4(c0, c1, c2, c3);
 }
 
-__device__ __forceinline__ uint32_t sr_e4m3(float in, uint32_t noise16) {
+// The value whose round-to-nearest E4M3 conversion is the stochastic rounding
+// of `in` with 16 bits of noise: inside E4M3's normal range the 20 mantissa
+// bits below E4M3's 3 are truncated or rounded up against the noise; outside
+// it (saturation, subnormals) `in` is converted as it is.
+__device__ __forceinline__ float sr_e4m3_pre(float in, uint32_t noise16) {
   const float a = fabsf(in);
-  if (a > 448.f || a < 0.015625f) return cvt_e4m3(in);
+  if (a > 448.f || a < 0.015625f) return in;
   const uint32_t mask = 0x000FFFFFu;
   const uint32_t threshold = (noise16 << 4) & mask;
   uint32_t bits = __float_as_uint(in);
   bits = ((bits & mask) > threshold) ? (bits | mask) : (bits & ~mask);
-  return cvt_e4m3(__uint_as_float(bits));
+  return __uint_as_float(bits);
+}
+
+// Two values -> two E4M3 bytes (lo in the low byte), round-to-nearest, saturating.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 h;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 h, %1, %2;\n\t"
+      "cvt.u32.u16 %0, h;\n\t}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Eight consecutive blocked scales: scratch group i -> sf group i.
@@ -561,14 +578,15 @@ __device__ __forceinline__ void sr8(uint2* __restrict__ sf, const uint4* __restr
   const uint4 rnd = philox4x32_10(seed, static_cast<uint32_t>(i));
   const uint32_t w[4] = {s.x, s.y, s.z, s.w};
   const uint32_t nz[4] = {rnd.x, rnd.y, rnd.z, rnd.w};
-  uint32_t o[2] = {0u, 0u};
+  float v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float v = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16)) * f;
-    const uint32_t noise = (j & 1) ? (nz[j >> 1] >> 16) : (nz[j >> 1] & 0xFFFFu);
-    o[j >> 2] |= sr_e4m3(v, noise) << (8 * (j & 3));
+    const float x = __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16)) * f;
+    v[j] = sr_e4m3_pre(x, (j & 1) ? (nz[j >> 1] >> 16) : (nz[j >> 1] & 0xFFFFu));
   }
-  __stcs(sf + i, make_uint2(o[0], o[1]));
+  const uint32_t o0 = cvt_e4m3x2(v[0], v[1]) | (cvt_e4m3x2(v[2], v[3]) << 16);
+  const uint32_t o1 = cvt_e4m3x2(v[4], v[5]) | (cvt_e4m3x2(v[6], v[7]) << 16);
+  __stcs(sf + i, make_uint2(o0, o1));
 }
 
 // Tensor scale from the global max and the reciprocal the SR pass multiplies by.
