@@ -49,6 +49,7 @@ SIGNATURES = {
     "q2b_quant_rows_fused": [_P, _P, _P, _P, _F, _I64, _I64, _INT, _P],
     "q2b_relu2_abs_max": [_P, _P, _P, _I64, _P],
     "q2b_relu2_bwd": [_P, _P, _P, _I64, _P],
+    "q2b_softmax_xent_bf16": [_P, _P, _P, _F, _I64, _I64, _P],
     "q2b_rope_norm_fwd": [_P, _P, _P, _P, _P, _I64, _INT, _INT, _P],
     "q2b_rope_norm_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _INT, _INT, _P],
     "q2b_add_rmsnorm_amax": [_P, _P, _P, _P, _P, _P, _P, _I64, _INT, _F, _P],

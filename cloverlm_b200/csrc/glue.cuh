@@ -330,4 +330,74 @@ __global__ void __launch_bounds__(256) relu2_bwd_kernel(uint4* da, const uint4* 
   }
 }
 
+// ------------------------------------------------- softmax cross-entropy rows
+// One CTA per row of bf16 logits [rows, V] (V a multiple of 8): an online
+// max / sum-of-exponentials pass gives lse = max + log(sum exp(x - max)), then
+// row_loss[r] = lse - x[t] and, in place, the gradient of the mean loss
+// bf16((exp(x - lse) - [j == t]) * inv_n) -- F.cross_entropy of the reference's
+// get_loss (src/data/utils_data.py:293-318) and its backward, for one chunk of
+// rows of the tied head, with one read and one write of the logits.
+constexpr int kXentThreads = 256;
+
+// (m, s) <- the running max and sum of exp(x - max) of the union of two parts
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  if (m2 > m) { s = s * expf(m - m2) + s2; m = m2; } else if (m2 != -INFINITY) { s += s2 * expf(m2 - m); }
+}
+
+__global__ void __launch_bounds__(kXentThreads) softmax_xent_kernel(uint4* logits, float* __restrict__ row_loss,
+                                                                    const int64_t* __restrict__ targets, float inv_n,
+                                                                    int64_t V) {
+  __shared__ float red_m[kXentThreads / 32], red_s[kXentThreads / 32];
+  __shared__ float lse_sh;
+  const int64_t row = blockIdx.x;
+  uint4* x = logits + row * (V / 8);
+  const int64_t nv = V / 8;
+  float m = -INFINITY, s = 0.f;
+  for (int64_t i = threadIdx.x; i < nv; i += kXentThreads) {
+    const uint4 v = x[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float lm = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) lm = fmaxf(lm, fmaxf(bf_lo(w[k]), bf_hi(w[k])));
+    float ls = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ls += expf(bf_lo(w[k]) - lm) + expf(bf_hi(w[k]) - lm);
+    online_merge(m, s, lm, ls);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red_m[warp] = m; red_s[warp] = s; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = red_m[0], S = red_s[0];
+    for (int k = 1; k < kXentThreads / 32; ++k) online_merge(M, S, red_m[k], red_s[k]);
+    const float lse = M + logf(S);
+    lse_sh = lse;
+    const int64_t t = targets[row];
+    const uint16_t tb = reinterpret_cast<const uint16_t*>(x)[t];
+    row_loss[row] = lse - __uint_as_float(static_cast<uint32_t>(tb) << 16);
+  }
+  __syncthreads();
+  const float lse = lse_sh;
+  const int64_t t = targets[row];
+  for (int64_t i = threadIdx.x; i < nv; i += kXentThreads) {
+    const uint4 v = x[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float p0 = expf(bf_lo(w[k]) - lse), p1 = expf(bf_hi(w[k]) - lse);
+      const int64_t j = i * 8 + 2 * k;
+      if (j == t) p0 -= 1.f;
+      if (j + 1 == t) p1 -= 1.f;
+      o[k] = pack_bf16x2(p0 * inv_n, p1 * inv_n);
+    }
+    x[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace q2b

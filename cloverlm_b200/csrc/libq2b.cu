@@ -315,6 +315,21 @@ int q2b_relu2_bwd(void* da, const void* a, const void* g, int64_t n, void* strea
   return Q2B_OK;
 }
 
+int q2b_softmax_xent_bf16(void* logits, float* row_loss, const int64_t* targets, float inv_n, int64_t rows, int64_t V,
+                          void* stream) {
+  Q2B_REQUIRE_PTR(logits);
+  Q2B_REQUIRE_NONNULL(row_loss);
+  Q2B_REQUIRE_NONNULL(targets);
+  if (rows <= 0 || rows >= (int64_t(1) << 31)) return fail(Q2B_ERR_INVALID, "softmax_xent: rows must be in [1, 2^31)");
+  if (V <= 0 || V % 8 != 0) return fail(Q2B_ERR_INVALID, "softmax_xent: V must be a positive multiple of 8");
+  int dev, sms;
+  if (int r = device_setup(&dev, &sms)) return r;
+  q2b::softmax_xent_kernel<<<static_cast<unsigned>(rows), q2b::kXentThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(logits), row_loss, targets, inv_n, V);
+  Q2B_CUDA(cudaGetLastError());
+  return Q2B_OK;
+}
+
 int q2b_watchdog_poll(unsigned* host_word, void* stream) {
   Q2B_REQUIRE_NONNULL(host_word);
   Q2B_CUDA(cudaMemcpyFromSymbolAsync(host_word, q2b::g_watchdog, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,

@@ -201,13 +201,14 @@ class _TiedHeadCrossEntropy(torch.autograd.Function):
         inv_n = 1.0 / n
         for s in range(0, n, _TiedHeadCrossEntropy.CHUNK):
             e = min(n, s + _TiedHeadCrossEntropy.CHUNK)
-            logits = (hb[s:e] @ wb.T).float()
-            lse = torch.logsumexp(logits, dim=1)
-            t = targets[s:e]
-            total += (lse - logits.gather(1, t[:, None]).squeeze(1)).sum()
-            p = logits.sub_(lse[:, None]).exp_()
-            p[torch.arange(e - s, device=p.device), t] -= 1.0
-            g = p.mul_(inv_n).to(torch.bfloat16)
+            # bf16 logits; q2b_softmax_xent_bf16 reads them once in fp32, writes each row's
+            # loss and replaces the logits by the gradient of the mean loss (bf16)
+            g = hb[s:e] @ wb.T
+            row_loss = torch.empty(e - s, dtype=torch.float32, device=h.device)
+            t = targets[s:e].to(torch.int64).contiguous()
+            _lib.call("q2b_softmax_xent_bf16", _lib.ptr(g), _lib.ptr(row_loss), _lib.ptr(t), inv_n, e - s, g.shape[1],
+                      _lib.stream_of(g))
+            total += row_loss.sum()
             dh[s:e] = g @ wb
             # bf16 operands, fp32 accumulation into dw in the GEMM itself
             dw = torch.addmm(dw, g.T, hb[s:e], out_dtype=torch.float32)

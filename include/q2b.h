@@ -283,6 +283,14 @@ int q2b_rmsnorm_bwd(float* dx, void* dy, float* dw_partial, int64_t partial_rows
  * Replaces: the autograd backward of relu(x)**2, src/models/mlp.py:34-38. */
 int q2b_relu2_bwd(void* da, const void* a, const void* g, int64_t n, void* stream);
 
+/* Cross-entropy of rows of bf16 logits [rows, V] (V a multiple of 8) against int64 targets:
+ * row_loss[r] = logsumexp(x_r) - x_r[t_r] (fp32), and the logits are overwritten with the
+ * gradient of inv_n * sum(row_loss): bf16((softmax(x_r) - onehot(t_r)) * inv_n).
+ * Replaces: F.cross_entropy of get_loss (src/data/utils_data.py:293-318) and its autograd
+ * backward, applied per chunk of rows of the tied output head. */
+int q2b_softmax_xent_bf16(void* logits, float* row_loss, const int64_t* targets, float inv_n, int64_t rows, int64_t V,
+                          void* stream);
+
 /* Measurement: one SM pair per two SMs issues `iters` back-to-back
  * cta_group::2 M256 N256 K64 NVFP4 block-scaled MMAs on operands resident in
  * shared memory (2*256*256*64 FLOP each; total FLOP = (SMs/2) * iters * that).

@@ -183,3 +183,22 @@ def test_training_steps_lower_the_loss():
     for blk in model.blocks:  # the optimizer keeps the Quartet layers' weight abs-max current
         for lin in (blk.lq, blk.lk, blk.lv, blk.lo, blk.l1, blk.l2):
             assert lin.weight_abs_max.item() == lin.weight.detach().to(torch.bfloat16).float().abs().max().item()
+
+
+@pytest.mark.parametrize("rows,V", [(300, 1000), (64, 32768), (3, 8)])
+def test_softmax_xent_kernel_matches_torch(rows, V):
+    torch.manual_seed(5)
+    x = (torch.randn(rows, V, device="cuda") * 4).to(torch.bfloat16)
+    t = torch.randint(0, V, (rows,), device="cuda")
+    inv_n = 1.0 / 777
+    g = x.clone()
+    row_loss = torch.empty(rows, dtype=torch.float32, device="cuda")
+    _lib.call("q2b_softmax_xent_bf16", _lib.ptr(g), _lib.ptr(row_loss), _lib.ptr(t), inv_n, rows, V, _lib.stream_of(g))
+    xf = x.float().requires_grad_()
+    ref = F.cross_entropy(xf, t, reduction="none")
+    torch.testing.assert_close(row_loss, ref.detach(), rtol=1e-5, atol=1e-5)
+    (ref.sum() * inv_n).backward()
+    want = xf.grad.to(torch.bfloat16)
+    # the same fp32 formula up to the reduction order of the log-sum-exp: equal or one bf16 step apart
+    diff = (g.float() - want.float()).abs()
+    assert (diff <= want.float().abs() * 2 ** -7 + 1e-12).all()
