@@ -38,6 +38,7 @@ struct GemmParams {
   int splits;           // K split into this many ranges per output tile (1 = none)
   float* ws;            // splits > 1: fp32 partial tiles [tiles][128][BN], zero between calls
   unsigned* counters;   // splits > 1: arrival counters [tiles][epilogue warps], zero between calls
+  int raster_rows = 1;  // pair kernel: row tiles per raster group (1 = row-major tile order)
 };
 
 template <int BN>
@@ -462,6 +463,21 @@ struct Gemm2Cfg {
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
+// Output tile t -> (row tile, column tile) in groups of `group` row tiles:
+// consecutive tiles (the CTAs of one wave) walk a group's rows fastest, so a
+// wave touches about `group` A panels and 74 / group B panels instead of
+// 74 / tiles_n A panels and all tiles_n B panels; with long K the panels a
+// wave streams then fit L2 together.  group = 1 is row-major order.
+__device__ __forceinline__ void tile_coords(int64_t t, int64_t tiles_m, int64_t tiles_n, int64_t group, int64_t& tm,
+                                            int64_t& tn) {
+  const int64_t per = group * tiles_n;
+  const int64_t grp = t / per, in = t - grp * per;
+  const int64_t m0 = grp * group;
+  const int64_t gs = tiles_m - m0 < group ? tiles_m - m0 : group;
+  tm = m0 + in % gs;
+  tn = in / gs;
+}
+
 #ifdef Q2B_GEMM2_STATS
 // Instrumented builds only: cycle counts of CTA 0's roles (0 MMA: total, 1 MMA: waiting for
 // scales, 2 MMA: waiting for the accumulator, 3 K blocks, 4 copy warp 0: waiting for stages,
@@ -533,7 +549,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   const bool leader = rank == 0;
   const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const int64_t tiles_n = p.N / 256;
-  const int64_t ntiles = (p.M / 256) * tiles_n;
+  const int64_t tiles_m = p.M / 256;
+  const int64_t ntiles = tiles_m * tiles_n;
   const int64_t nkb = (p.K + 255) / 256;
   const int64_t n_kt = p.K / 64;
   const int tail_nk = static_cast<int>((p.K % 256) / 64);
@@ -577,7 +594,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     int64_t it = 0;
     bool ok = true;
     for (int64_t t = cluster_id; t < ntiles && ok; t += nclusters) {
-      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      int64_t tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.raster_rows, tm, tn);
       const int a_row = static_cast<int>(tm * 256 + rank * 128);
       const int b_row = static_cast<int>(tn * 256 + rank * 128);
       const int64_t sfa_chunk0 = (tm * 2 + rank) * n_kt;
@@ -709,7 +727,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
     int64_t tc = 0;
     for (int64_t t = cluster_id; t < ntiles; t += nclusters, ++tc) {
       // tile coordinates before the wait: the drain is on the MMA's critical path
-      const int64_t tm = t / tiles_n, tn = t % tiles_n;
+      int64_t tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.raster_rows, tm, tn);
       const int row0 = static_cast<int>(tm * 256 + rank * 128 + q * 32);
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + c0;
       Q2B_S_T(_e0)

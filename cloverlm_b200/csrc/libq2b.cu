@@ -785,7 +785,10 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
   if (int r = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, m_valid, 128, 128)) return r;
 #ifndef Q2B_GEMM_NO_2SM
   if (takes_pair_kernel(m_valid, N, sms, D)) {
-    // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair; D written by TMA stores
+    // 2-SM pairs: 256x256 tiles, one cluster of two CTAs per SM pair; D written by TMA stores.
+    // Long K: tiles in groups of 8 row tiles, so one wave's K panels fit L2 (a 256-row panel
+    // is 128 x K bytes: 2 MB at K = 16384, and row-major waves touch every column panel)
+    p.raster_rows = K >= 16384 ? 8 : 1;
     CUtensorMap tsa, tsb, td;
     // store boxes of 32 rows x 64 bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle
     CUtensorMap td2;
