@@ -59,7 +59,6 @@ struct RhtParams {
 };
 
 
-constexpr int kRhtStages = 4;
 constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one bf16 tile
 constexpr uint32_t kHalfBytes = 128 * 128;      // one 64-column half of a tile
 
@@ -91,9 +90,12 @@ struct RhtCfg {
   // NVFP4 input ring: per stage the tile's codes (128 rows x 64 bytes) and its
   // two 512-byte blocks of scales
   static constexpr int kRawStages = (kIn == kInFp4) ? 4 : 0;
+  // bf16 tiles in the ring: three for bf16 input (measured: 4, 5 and 6 stages
+  // run slower -- more shared memory in flight and less L1 did not buy bandwidth)
+  static constexpr int kStages = (kIn == kInBf16) ? 3 : 4;
   static constexpr uint32_t kRawBytes = 128 * 64 + 1024;
   // shared memory: [H 32K][stages x 32K][raw stages x 9K][barriers]
-  static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kRhtStages) + kRawStages * kRawBytes + 256;
+  static constexpr uint32_t kSmemBytes = 1024 + kTileBytes * (1 + kStages) + kRawStages * kRawBytes + 256;
 };
 
 // Byte offset of bf16 element (r, c) of a 128x128 tile stored as two 64-column
@@ -192,10 +194,10 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* hs = smem;
   uint8_t* tiles = smem + kTileBytes;
-  uint8_t* raw = tiles + kRhtStages * kTileBytes;  // NVFP4 input ring
+  uint8_t* raw = tiles + Cfg::kStages * kTileBytes;  // NVFP4 input ring
   uint64_t* full = reinterpret_cast<uint64_t*>(raw + Cfg::kRawStages * Cfg::kRawBytes);
-  uint64_t* empty = full + kRhtStages;
-  uint64_t* tfull = empty + kRhtStages;
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* tfull = empty + Cfg::kStages;
   uint64_t* tempty = tfull + 4;
   uint64_t* drain = tempty + 4;  // the MMA warp's final commit: no MMA in flight at dealloc
   uint64_t* rfull = drain + 1;  // NVFP4 input ring: codes + scales landed
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
 #endif
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRhtStages; ++s) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], kIn == kInBf16 ? 1 : 32 * Cfg::kConvWarps);
       mbar_init(&empty[s], 1);
     }
@@ -246,8 +248,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         const uint64_t policy = policy_evict_first();
         int it = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-          const int slot = it % kRhtStages;
-          const uint32_t ph = (it / kRhtStages) & 1;
+          const int slot = it % Cfg::kStages;
+          const uint32_t ph = (it / Cfg::kStages) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
           const uint32_t t32 = static_cast<uint32_t>(t);
           const int tm = static_cast<int>(t32 / tiles_n), tn = static_cast<int>(t32 % tiles_n);
@@ -258,8 +260,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
         }
         // drain: make sure no copy is still landing when the CTA retires
         const int issued = it;
-        for (int k = issued > kRhtStages ? issued - kRhtStages : 0; k < issued; ++k)
-          mbar_wait(&full[k % kRhtStages], (k / kRhtStages) & 1, kTimeoutProducer);
+        for (int k = issued > Cfg::kStages ? issued - Cfg::kStages : 0; k < issued; ++k)
+          mbar_wait(&full[k % Cfg::kStages], (k / Cfg::kStages) & 1, kTimeoutProducer);
       }
     } else if (warp == Cfg::kLoadWarp) {
       // NVFP4 input, loader: the tile's 128 x 64 code bytes by TMA and its two
@@ -312,8 +314,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
                                                                        (((r >> 5) & 3) << 2) | (kb & 3)));
         }
         mbar_arrive(&rempty[rs]);
-        const int slot = it % kRhtStages;
-        const uint32_t ph = (it / kRhtStages) & 1;
+        const int slot = it % Cfg::kStages;
+        const uint32_t ph = (it / Cfg::kStages) & 1;
         Q2B_R_T(_p1)
         if (!mbar_wait(&empty[slot], ph ^ 1, kTimeoutSmemEmpty)) break;
         Q2B_R_T(_p2)
@@ -360,8 +362,8 @@ __global__ void __launch_bounds__(RhtCfg<kIn, kOut>::kThreads, 1)
     bool ok = true;
     Q2B_R_T(_ml)
     for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-      const int slot = it % kRhtStages;
-      const uint32_t ph = (it / kRhtStages) & 1;
+      const int slot = it % Cfg::kStages;
+      const uint32_t ph = (it / Cfg::kStages) & 1;
       const int buf = it % Cfg::kTmemBufs;
       const uint32_t bph = (it / Cfg::kTmemBufs) & 1;
       Q2B_R_T(_m0)
