@@ -127,10 +127,16 @@ __global__ void __launch_bounds__(256) quant_fwd_v2_kernel(uint2* __restrict__ c
   // whole warps stay in the loop (the scale gather below shuffles across the
   // warp); lanes past the end load nothing and store nothing
   const uint32_t ngroups_up = (ngroups + 31u) & ~31u;
-  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < ngroups_up; g += stride) {
+  // the next group's 32 bytes are loaded while this one is quantized
+  uint32_t wn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g0 < ngroups) ldg256(x + static_cast<uint64_t>(g0) * 16, wn);
+  for (uint32_t g = g0; g < ngroups_up; g += stride) {
     const bool valid = g < ngroups;
-    uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (valid) ldg256(x + static_cast<uint64_t>(g) * 16, w);
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = wn[k];
+    if (static_cast<uint64_t>(g) + stride < ngroups) ldg256(x + (static_cast<uint64_t>(g) + stride) * 16, wn);
     float xs[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
