@@ -3,7 +3,8 @@
 the test short; Q2B_REF_SPEED_TOKENS sets another count): the reference's quantizer kernels
 built from its sources (oracle/_ref/libq2ref.so, see oracle/Makefile) plus FlashInfer's cuDNN NVFP4 GEMM, composed as Quartet_II_fn does
 (quartet2/python/quartet2/linear.py:155-233), against cloverlm_b200's kernels.  Prints the
-per-op table (run with -s); asserts only that both paths ran and ours is not slower than 1.5x."""
+per-op table of device times (run with -s); asserts only that both paths ran and ours is not slower
+than 1.5x."""
 import ctypes
 import os
 
@@ -18,16 +19,20 @@ SHAPES = [("qkv", 3584, 10752), ("attn_out", 3584, 3584), ("mlp_up", 3584, 14336
 
 
 def _timed(fn, reps=5):
+    """Device time of one call in ms: the summed duration of the kernels (and memsets) the call
+    launches, from the torch profiler's CUDA activity.  Both paths are launched from Python with
+    different host overheads, so wall-clock time between events would time the host for the
+    smaller tensors."""
+    from torch.profiler import ProfilerActivity, profile
     for _ in range(2):
         fn()
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        fn()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) / reps
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    us = sum(e.device_time_total for e in prof.events() if e.device_type.name == "CUDA")
+    return us / 1e3 / reps
 
 
 def test_reference_gpu_path_vs_ours():
