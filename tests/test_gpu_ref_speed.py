@@ -140,6 +140,7 @@ def test_gemm_per_shape_against_cudnn():
     from cloverlm_b200.quant import NVFP4QuantMode, quant_fp4
     M = int(os.environ.get("Q2B_REF_SPEED_TOKENS", "16384"))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    warm = os.environ.get("Q2B_REF_SPEED_WARM") == "1"  # keep L2 between calls (operands resident)
 
     def q(r, c, seed):
         g = torch.Generator(device="cuda").manual_seed(seed)
@@ -151,7 +152,8 @@ def test_gemm_per_shape_against_cudnn():
         torch.cuda.synchronize()
         ts = []
         for _ in range(reps):
-            flush.zero_()
+            if not warm:
+                flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
