@@ -78,12 +78,15 @@ struct RhtCfg {
   // (one per TMEM lane quarter, per orientation) take tiles in turn too; the
   // number of groups divides the number of buffers.
   static constexpr int kTmemBufs = (kNumOut == 2) ? 2 : 4;
-  static constexpr int kEpiWarps = (kIn == kInFp4) ? 24 - kConvWarps : 16;
+  static constexpr int kEpiWarps = 16;
   static constexpr int kEpiGroups = kEpiWarps / (4 * kNumOut);
   static_assert(kTmemBufs % kEpiGroups == 0, "groups must divide buffers");
   static constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
   static constexpr uint32_t kColsPerBuf = 128 * kNumOut;
-  static constexpr uint32_t kTmemCols = kTmemBufs * kColsPerBuf;  // 512
+  // tcgen05.alloc takes a power of two of at least 32 columns
+  static constexpr uint32_t kTmemUsed = kTmemBufs * kColsPerBuf;
+  static constexpr uint32_t kTmemCols = kTmemUsed <= 128 ? 128 : (kTmemUsed <= 256 ? 256 : 512);
+  static_assert(kTmemUsed <= 512, "TMEM overflow");
   // columns per TMEM load of a one-orientation epilogue warp, double-buffered:
   // 16 keeps the 800-thread requant block within 80 registers a thread
   static constexpr int kLdCols = (kIn == kInFp4) ? 16 : 32;
