@@ -548,8 +548,8 @@ __global__ void __launch_bounds__(Gemm2Cfg::kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-  const int64_t tiles_n = p.N / 256;
-  const int64_t tiles_m = p.M / 256;
+  const int64_t tiles_n = (p.N + 255) / 256;  // a last half tile reads zeros and stores nothing past N
+  const int64_t tiles_m = (p.M + 255) / 256;
   const int64_t ntiles = tiles_m * tiles_n;
   const int64_t nkb = (p.K + 255) / 256;
   const int64_t n_kt = p.K / 64;

@@ -763,9 +763,12 @@ int64_t split_ws_bytes(const SplitPlan& sp) {
 }
 
 // Whether the 2-SM pair kernel takes this problem (256-aligned, enough tiles to fill the pairs).
+// The pair kernel covers M and N in 256-wide tiles; a last half tile (M or N = 128 mod 256) is
+// read as zeros past the end by TMA (A, B and both scale maps are bounded by the real extent)
+// and its stores are clipped to the real extent, so multiples of 128 suffice.
 bool takes_pair_kernel(int64_t m_valid, int64_t N, int sms, const void* D) {
   const int64_t M = (m_valid + 127) / 128 * 128;
-  return m_valid % 256 == 0 && N % 256 == 0 && sms >= 2 && (M / 256) * (N / 256) * 2 >= sms &&
+  return m_valid % 128 == 0 && N % 128 == 0 && sms >= 2 && ((M + 255) / 256) * ((N + 255) / 256) * 2 >= sms &&
          (reinterpret_cast<uintptr_t>(D) & 15u) == 0;
 }
 
@@ -812,7 +815,7 @@ int gemm_launch(void* D, const void* A, const void* B, const void* sfa, const vo
     if (int r = make_tmap(&tsb, sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, N * K / 16 / 256, 256, 8,
                           CU_TENSOR_MAP_SWIZZLE_NONE))
       return r;
-    const int64_t tiles = (M / 256) * (N / 256);
+    const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
     const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];

@@ -69,9 +69,11 @@ def test_gemm_blocky_scales(M, N, K):
     _check(M, N, K, seed=7, blocky=True)
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 3584, 3584), (2048, 2560, 1408), (2048, 2560, 8192), (2560, 2048, 640)])
+@pytest.mark.parametrize("M,N,K", [(4096, 3584, 3584), (2048, 2560, 1408), (2048, 2560, 8192), (2560, 2048, 640),
+                                   (4096, 896, 3584), (896, 3584, 8192), (2176, 2688, 1408)])
 def test_gemm_pair_kernel_shapes(M, N, K):
-    """Shapes whose 256x256 tiles fill the SM pairs take the cta_group::2 kernel (ragged K tails included)."""
+    """Shapes whose 256x256 tiles fill the SM pairs take the cta_group::2 kernel (ragged K tails included;
+    M or N = 128 mod 256 leave a half tile read as zeros and clipped on store)."""
     rel = _check(M, N, K, seed=M + K)
     assert rel < 5e-3
 
@@ -162,3 +164,23 @@ def test_gemm_add_accumulates_into_the_output(M, N, K):
     diff = (got.view(torch.int16).int() - want.view(torch.int16).int()).abs()
     assert int(diff.max()) <= 1 and (diff != 0).float().mean().item() <= 1e-3
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(32768, 896, 3584), (896, 3584, 32768), (2176, 2688, 1408)])
+def test_gemm_half_tiles_bit_identical_to_cudnn(M, N, K):
+    """The pair kernel with a half last tile (the GQA K/V projections' 896 columns or rows) gives the
+    same bits as the reference's GEMM (FlashInfer's cuDNN NVFP4 path)."""
+    mm_fp4 = pytest.importorskip("flashinfer").mm_fp4
+    from cloverlm_b200.quant import NVFP4QuantMode, quant_fp4
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = quant_fp4(torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16), scale_override=1.0,
+                  mode=NVFP4QuantMode.FOUR_SIX)
+    B = quant_fp4(torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16), scale_override=1.0,
+                  mode=NVFP4QuantMode.FOUR_SIX)
+    alpha = A.tensor_scale * B.tensor_scale
+    ours = _fp4_mm(A.fp4, B.fp4, A.micro_scales, B.micro_scales, alpha)
+    ref = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    mm_fp4(A.fp4, B.fp4.T, A.micro_scales.view(torch.float8_e4m3fn).view(-1, K // 16),
+           B.micro_scales.view(torch.float8_e4m3fn).view(-1, K // 16).T, alpha, torch.bfloat16, ref, block_size=16,
+           use_8x4_sf_layout=False, backend="cudnn", use_nvfp4=True)
+    assert torch.equal(ours, ref)
