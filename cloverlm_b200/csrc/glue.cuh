@@ -173,12 +173,18 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_amax_kernel(
   float m = 0.f;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     uint4 yv[kNormMaxVecs];
+    float4 xv[kNormMaxVecs][2];  // the residual's 8 values, loaded before the reduction needs them
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < kNormMaxVecs; ++k) {
       const int c = threadIdx.x + k * kNormThreads;
       yv[k] = make_uint4(0, 0, 0, 0);
-      if (c < nv) yv[k] = __ldcs(y + r * nv + c);
+      if (c < nv) {
+        yv[k] = __ldcs(y + r * nv + c);
+        const float4* xp = reinterpret_cast<const float4*>(x + (r * nv + c) * 8);
+        xv[k][0] = __ldcs(xp);
+        xv[k][1] = __ldcs(xp + 1);
+      }
       const uint32_t a[4] = {yv[k].x, yv[k].y, yv[k].z, yv[k].w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -192,9 +198,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_amax_kernel(
     for (int k = 0; k < kNormMaxVecs; ++k) {
       const int c = threadIdx.x + k * kNormThreads;
       if (c >= nv) continue;
-      const float4* xp = reinterpret_cast<const float4*>(x + (r * nv + c) * 8);
       const float4* wp = reinterpret_cast<const float4*>(w + c * 8);
-      const float4 x0 = __ldcs(xp), x1 = __ldcs(xp + 1);
+      const float4 x0 = xv[k][0], x1 = xv[k][1];
       const float4 w0 = wp[0], w1 = wp[1];
       const uint32_t a[4] = {yv[k].x, yv[k].y, yv[k].z, yv[k].w};
       const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
