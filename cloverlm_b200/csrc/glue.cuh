@@ -42,9 +42,10 @@ __global__ void __launch_bounds__(kRopeThreads) rope_norm_fwd_kernel(
     const bool ok = v < nvec;
     uint4 w = make_uint4(0, 0, 0, 0);
     if (ok) w = __ldcs(x + v * 16 + lane);
-    const int64_t row = v / H;
+    // head vectors stay below 2^31 (the launchers check): 32-bit division, not a 64-bit one
+    const uint32_t row = static_cast<uint32_t>(v) / static_cast<uint32_t>(H);
     const int h = static_cast<int>(v - row * H);
-    const int pos = static_cast<int>(row % seq);
+    const int pos = static_cast<int>(row % static_cast<uint32_t>(seq));
     const uint32_t win[4] = {w.x, w.y, w.z, w.w};
     float y[8];
     float ss = 0.f;
@@ -91,17 +92,25 @@ __global__ void __launch_bounds__(kRopeThreads) rope_norm_bwd_kernel(
   __syncthreads();
   const int lane = threadIdx.x & 15;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * (kRopeThreads / 16);
+  // the next head vector's gradient and output are loaded while this one is processed
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * (kRopeThreads / 16) + (threadIdx.x >> 4);
+  uint4 gn = make_uint4(0, 0, 0, 0), on = make_uint4(0, 0, 0, 0);
+  if (first < nvec) {
+    gn = __ldcs(dout + first * 16 + lane);
+    on = __ldcs(out + first * 16 + lane);
+  }
   for (int64_t v0 = static_cast<int64_t>(blockIdx.x) * (kRopeThreads / 16); v0 < nvec; v0 += stride) {
     const int64_t v = v0 + (threadIdx.x >> 4);
     const bool ok = v < nvec;
-    uint4 g = make_uint4(0, 0, 0, 0), o = make_uint4(0, 0, 0, 0);
-    if (ok) {
-      g = __ldcs(dout + v * 16 + lane);
-      o = __ldcs(out + v * 16 + lane);
+    const uint4 g = gn, o = on;
+    if (v + stride < nvec) {
+      gn = __ldcs(dout + (v + stride) * 16 + lane);
+      on = __ldcs(out + (v + stride) * 16 + lane);
     }
-    const int64_t row = v / H;
+    // head vectors stay below 2^31 (the launchers check): 32-bit division, not a 64-bit one
+    const uint32_t row = static_cast<uint32_t>(v) / static_cast<uint32_t>(H);
     const int h = static_cast<int>(v - row * H);
-    const int pos = static_cast<int>(row % seq);
+    const int pos = static_cast<int>(row % static_cast<uint32_t>(seq));
     const float s = (scale != nullptr && ok) ? scale[h] : 1.f;
     const float inv_s = 1.f / s;
     const float d = ok ? norm[v] : 1.f;

@@ -221,6 +221,7 @@ int q2b_rope_norm_fwd(void* out, float* norm_out, const void* x, const float* co
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   const int64_t nvec = rows * heads;
+  if (nvec >= (int64_t(1) << 31)) return fail(Q2B_ERR_INVALID, "rope_norm: rows * heads must be below 2^31");
   const int64_t blocks = std::min<int64_t>((nvec + 15) / 16, static_cast<int64_t>(sms) * 16);
   q2b::rope_norm_fwd_kernel<<<static_cast<unsigned>(blocks), q2b::kRopeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(out), norm_out, static_cast<const uint4*>(x), reinterpret_cast<const float2*>(cos_sin),
@@ -243,6 +244,7 @@ int q2b_rope_norm_bwd(void* dx, float* dscale, const void* dout, const void* out
   int dev, sms;
   if (int r = device_setup(&dev, &sms)) return r;
   const int64_t nvec = rows * heads;
+  if (nvec >= (int64_t(1) << 31)) return fail(Q2B_ERR_INVALID, "rope_norm: rows * heads must be below 2^31");
   const int64_t blocks = std::min<int64_t>((nvec + 15) / 16, static_cast<int64_t>(sms) * 8);
   q2b::rope_norm_bwd_kernel<<<static_cast<unsigned>(blocks), q2b::kRopeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(dx), dscale, static_cast<const uint4*>(dout), static_cast<const uint4*>(out), norm,
