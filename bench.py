@@ -648,6 +648,8 @@ KERNEL_CASES = {
     # name: (what, shape) -- single-kernel workloads of the training step's shapes, for ncu captures
     "gemm_fwd": "q2b_gemm_nvfp4 (pair kernel, bf16 out): MLP-down forward, M=32768 N=3584 K=14336",
     "gemm_wgrad": "q2b_gemm_nvfp4_f32 (pair kernel, fp32 out): MLP-up wgrad, M=14336 N=3584 K=32768",
+    "gemm_qkv_65k": "q2b_gemm_nvfp4 (pair kernel, bf16 out): config-3 fused-QKV forward, M=65536 N=10752 K=3584",
+    "gemm_up_wgrad_65k": "q2b_gemm_nvfp4 (pair kernel, bf16 out): config-3 MLP-up wgrad, M=14336 N=3584 K=65536",
     "eden_dual": "q2b_rht_eden_dual: E [32768, 14336] -> E and E^T",
     "requant": "q2b_rht_requant: NVFP4 X [32768, 14336] -> X^T",
     "quant_fwd": "q2b_quant_fwd four-over-six: [32768, 14336]",
@@ -679,6 +681,12 @@ def kernel_case(name: str, reps: int = 3) -> None:
     elif name == "gemm_wgrad":
         a, b = q(14336, 32768), q(3584, 32768)
         fn = lambda: _fp4_mm_f32(a.fp4, b.fp4, a.micro_scales, b.micro_scales, a.tensor_scale * b.tensor_scale)
+    elif name == "gemm_qkv_65k":
+        a, b = q(65536, 3584), q(10752, 3584)
+        fn = lambda: _fp4_mm(a.fp4, b.fp4, a.micro_scales, b.micro_scales, a.tensor_scale * b.tensor_scale)
+    elif name == "gemm_up_wgrad_65k":
+        a, b = q(14336, 65536), q(3584, 65536)
+        fn = lambda: _fp4_mm(a.fp4, b.fp4, a.micro_scales, b.micro_scales, a.tensor_scale * b.tensor_scale)
     elif name == "eden_dual":
         x = rnd(32768, 14336)
         fn = lambda: rht128_quant_eden_dual(h=h, x=x, seed=torch.tensor(1), seed_t=torch.tensor(2))
