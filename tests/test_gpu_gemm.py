@@ -126,7 +126,7 @@ def test_fp4_mma_peak_probe_runs_in_range():
 
 
 @pytest.mark.parametrize("M,N,K", [(2048, 2560, 1408), (4096, 3584, 2048), (896, 3584, 4096), (384, 256, 640),
-                                   (128, 896, 512)])
+                                   (128, 896, 512), (896, 14336, 4096), (16384, 896, 1024)])
 def test_gemm_fp32_output_is_the_unrounded_bf16_result(M, N, K):
     """q2b_gemm_nvfp4_f32 (fp32 D, for fp32 weight gradients) holds alpha * the fp32
     accumulator: rounded to bf16 it equals the bf16 GEMM bit for bit, and it is within
@@ -146,7 +146,7 @@ def test_gemm_fp32_output_is_the_unrounded_bf16_result(M, N, K):
     assert ((f32 - ref).norm() / ref.norm()).item() < 1e-4  # fp32 accumulation only
 
 
-@pytest.mark.parametrize("M,N,K", [(2048, 2560, 1408), (4096, 3584, 896), (384, 256, 640)])
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 1408), (4096, 3584, 896), (384, 256, 640), (2176, 2688, 1408)])
 def test_gemm_add_accumulates_into_the_output(M, N, K):
     """q2b_gemm_nvfp4_add: D += bf16(alpha * A B^T), each element the bf16 sum of the old value and
     the bf16 GEMM result (TMA reductions on the 2-SM path, bf16 adds on the 1-SM path): equal to
